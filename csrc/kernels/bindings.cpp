@@ -1,0 +1,54 @@
+// Python bindings of the sm_100a kernel library (hrm_text_b200._C).
+#include <torch/extension.h>
+
+namespace hrm {
+void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_t M, int64_t N, int64_t K,
+          int64_t epi, const at::Tensor& out, const c10::optional<at::Tensor>& out2,
+          const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& aux,
+          const c10::optional<at::Tensor>& positions, const c10::optional<at::Tensor>& cos_tab,
+          const c10::optional<at::Tensor>& sin_tab, int64_t rope_begin, int64_t rope_end, int64_t pair_offset,
+          const c10::optional<at::Tensor>& labels, const c10::optional<at::Tensor>& ce_max,
+          const c10::optional<at::Tensor>& ce_sum, const c10::optional<at::Tensor>& ce_arg,
+          const c10::optional<at::Tensor>& ce_tgt, bool stream_k);
+int64_t attn_schedule_capacity(int64_t T, int64_t n_cu);
+void attn_schedule(const at::Tensor& cu_seqlens, const at::Tensor& prefix_lens, bool causal, const at::Tensor& sched);
+void attn_fwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out, const at::Tensor& y,
+              const at::Tensor& lse);
+void attn_bwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
+              const at::Tensor& lse, const at::Tensor& dy, const at::Tensor& positions, const at::Tensor& cos_tab,
+              const at::Tensor& sin_tab, const at::Tensor& d_out, const at::Tensor& dsum, const at::Tensor& dq_acc,
+              const at::Tensor& dqkv);
+void rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& inj, const c10::optional<at::Tensor>& s_out,
+                 const at::Tensor& y, const at::Tensor& rstd, int64_t T, double eps);
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& s, const at::Tensor& rstd,
+                 const c10::optional<at::Tensor>& dres, const at::Tensor& dx, int64_t T);
+void embedding_fwd(const at::Tensor& ids, const at::Tensor& w, const at::Tensor& out, double scale);
+void embedding_bwd(const at::Tensor& ids, const at::Tensor& dout, const at::Tensor& gw, double scale);
+void ce_finalize(const at::Tensor& pmax, const at::Tensor& psum, const at::Tensor& parg, const at::Tensor& tgt,
+                 const at::Tensor& labels, const at::Tensor& lse, const at::Tensor& loss_rows,
+                 const at::Tensor& correct);
+void ce_dlogits(const at::Tensor& logits, const at::Tensor& lse, const at::Tensor& labels, const at::Tensor& grad);
+void adam_atan2(const at::Tensor& p, const at::Tensor& g, const c10::optional<at::Tensor>& m, const at::Tensor& v,
+                const c10::optional<at::Tensor>& ema, const c10::optional<at::Tensor>& out16, const at::Tensor& hyper,
+                double beta1, double beta2, double wd, double ema_decay);
+void cast_f32_bf16(const at::Tensor& src, const at::Tensor& dst);
+at::Tensor device_error_word();
+}  // namespace hrm
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "HRM-Text sm_100a kernels";
+  m.def("gemm", &hrm::gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("attn_schedule_capacity", &hrm::attn_schedule_capacity);
+  m.def("attn_schedule", &hrm::attn_schedule);
+  m.def("attn_fwd", &hrm::attn_fwd);
+  m.def("attn_bwd", &hrm::attn_bwd);
+  m.def("rmsnorm_fwd", &hrm::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &hrm::rmsnorm_bwd);
+  m.def("embedding_fwd", &hrm::embedding_fwd);
+  m.def("embedding_bwd", &hrm::embedding_bwd);
+  m.def("ce_finalize", &hrm::ce_finalize);
+  m.def("ce_dlogits", &hrm::ce_dlogits);
+  m.def("adam_atan2", &hrm::adam_atan2);
+  m.def("cast_f32_bf16", &hrm::cast_f32_bf16);
+  m.def("device_error_word", &hrm::device_error_word);
+}

@@ -1,0 +1,604 @@
+// Persistent warp-specialised bf16 GEMM on 5th-generation tensor cores (tcgen05, sm_100a).
+//
+//   D[M, N] = sum_k A(m, k) * B(n, k)       (fp32 accumulation in TMEM)
+//
+// Operands are row-major tensors; each may be "K-major" (reduction dim contiguous) or
+// "MN-major" (output dim contiguous), which covers the three GEMMs of a linear layer:
+//   forward  Y  = X  W^T : A = X [M,K]  K-major,  B = W [N,K]  K-major
+//   dgrad    dX = dY W   : A = dY [M,N] K-major,  B = W [N,K]  MN-major (as [red, out])
+//   wgrad    dW = dY^T X : A = dY [T,N] MN-major, B = X [T,K]  MN-major
+//
+// CTA tile 128 x 256 x 64, 4-stage TMA ring (48 KB / stage, 128B swizzle), one CTA per SM.
+// Warp roles (192 threads):
+//   warp 0      : TMA producer (one elected lane)
+//   warp 1      : TMEM allocator + UMMA issuer (one elected lane)
+//   warps 2..5  : epilogue; TMEM lane quarter = warp % 4, one accumulator row per thread
+// The accumulator is double-buffered in TMEM (2 x 256 columns), so the epilogue of tile i
+// overlaps the main loop of tile i+1.
+//
+// Work split: whole tiles strided over CTAs, or (fp32 atomic epilogue only) an even split of
+// the flattened (tile, k-block) iteration space over CTAs ("stream-K"), which keeps every SM
+// busy for the small-output / long-K weight-gradient GEMMs.
+//
+// Epilogues (fused; one pass over the accumulator):
+//   STORE     out bf16 = acc
+//   RESIDUAL  out bf16 = acc + residual
+//   F32ADD    out fp32 += acc (atomic, stream-K)
+//   ROPE      out bf16 = acc, with rotate-half RoPE on the q/k head columns
+//   SWIGLU    B rows are gate/up pairs; writes gate|up and silu(gate)*up
+//   SWIGLU_BWD acc = dh; reads gate|up, writes d(gate)|d(up)
+//   CE        out bf16 logits + per-row partial (max, sum exp, argmax, target logit)
+//
+// All mbarrier waits are bounded (common.cuh); on a timeout the kernel records an error,
+// drains its own TMA loads and UMMAs, frees TMEM and returns.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace hrm {
+
+enum GemmEpilogue : int {
+  EPI_STORE = 0,
+  EPI_RESIDUAL = 1,
+  EPI_F32ADD = 2,
+  EPI_ROPE = 3,
+  EPI_SWIGLU = 4,
+  EPI_SWIGLU_BWD = 5,
+  EPI_CE = 6,
+};
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
+constexpr int GEMM_THREADS = 192;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int GEMM_SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256;
+
+struct GemmArgs {
+  int M, N, K;
+  void* out;
+  long ldo;
+  const __nv_bfloat16* residual;
+  long ldr;
+  void* out2;
+  long ldo2;
+  const __nv_bfloat16* aux;
+  long ldaux;
+  // RoPE (head_dim 128): fp32 tables [max_pos, 64]
+  const int* positions;
+  const float* cos_tab;
+  const float* sin_tab;
+  int rope_begin, rope_end;
+  // SwiGLU: offset of the "up" half (rows of B in fwd, columns of gate|up in bwd)
+  int pair_offset;
+  // cross-entropy partials, [n_tiles, M]
+  const int* labels;
+  float* ce_max;
+  float* ce_sum;
+  int* ce_arg;
+  float* ce_tgt;
+  int* err;
+  int stream_k;
+};
+
+struct TileSched {
+  int m_tiles, n_tiles, nk;
+  __device__ int tiles() const { return m_tiles * n_tiles; }
+};
+
+// Iterate the (tile, kb0, kb1) segments this CTA owns; identical in every role.
+template <typename F>
+__device__ __forceinline__ void for_each_segment(const TileSched& s, bool stream_k, F&& f) {
+  const int total_tiles = s.tiles();
+  if (!stream_k) {
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      if (!f(t, 0, s.nk)) return;
+    }
+    return;
+  }
+  const long long total = (long long)total_tiles * s.nk;
+  const long long begin = total * blockIdx.x / gridDim.x;
+  const long long end = total * (blockIdx.x + 1) / gridDim.x;
+  long long pos = begin;
+  while (pos < end) {
+    const int t = (int)(pos / s.nk);
+    const int kb0 = (int)(pos % s.nk);
+    const int kb1 = (int)min((long long)s.nk, kb0 + (end - pos));
+    if (!f(t, kb0, kb1)) return;
+    pos += kb1 - kb0;
+  }
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+    w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+    w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+    w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+    d[q] = w;
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32]) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w = s[q];
+    float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z), d = unpack_bf16x2(w.w);
+    v[8 * q + 0] = a.x; v[8 * q + 1] = a.y; v[8 * q + 2] = b.x; v[8 * q + 3] = b.y;
+    v[8 * q + 4] = c.x; v[8 * q + 5] = c.y; v[8 * q + 6] = d.x; v[8 * q + 7] = d.y;
+  }
+}
+
+__device__ __forceinline__ void tmem_load_f32x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(taddr, r);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+template <int A_MN, int B_MN, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  TileSched sched;
+  sched.m_tiles = (args.M + BM - 1) / BM;
+  sched.n_tiles = (EPI == EPI_SWIGLU) ? (args.N + 127) / 128 : (args.N + BN - 1) / BN;
+  sched.nk = (args.K + BK - 1) / BK;
+  const bool stream_k = (EPI == EPI_F32ADD) && args.stream_k;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    mbar_init(drain_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      int issued_round[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) issued_round[s] = -1;
+      bool ok = true;
+      for_each_segment(sched, stream_k, [&](int tile, int kb0, int kb1) -> bool {
+        const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES, r = it / STAGES;
+          if (!mbar_wait(&empty_bar[s], (r & 1) ^ 1)) {
+            report_error(args.err, kErrGemmWaitTimeout, 1);
+            ok = false;
+            return false;
+          }
+          mbar_arrive_expect_tx(&full_bar[s], A_STAGE_BYTES + B_STAGE_BYTES);
+          uint8_t* a_dst = sA + s * A_STAGE_BYTES;
+          uint8_t* b_dst = sB + s * B_STAGE_BYTES;
+          if (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full_bar[s], kb * BK, mt * BM);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full_bar[s], mt * BM, kb * BK);
+            tma_load_2d(a_dst + 8192, &tmA, &full_bar[s], mt * BM + 64, kb * BK);
+          }
+          if (!B_MN) {
+            int r0, r1;
+            if (EPI == EPI_SWIGLU) {
+              r0 = nt * 128;
+              r1 = args.pair_offset + nt * 128;
+            } else {
+              r0 = nt * BN;
+              r1 = nt * BN + 128;
+            }
+            tma_load_2d(b_dst, &tmB, &full_bar[s], kb * BK, r0);
+            tma_load_2d(b_dst + 16384, &tmB, &full_bar[s], kb * BK, r1);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[s], nt * BN + j * 64, kb * BK);
+          }
+          issued_round[s] = r;
+        }
+        return true;
+      });
+      if (!ok) {
+        // Drain: wait (bounded) until every load this thread issued has landed.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_round[s] >= 0) mbar_wait(&full_bar[s], issued_round[s] & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+      int it = 0, local = 0;
+      for_each_segment(sched, stream_k, [&](int tile, int kb0, int kb1) -> bool {
+        const int acc = local & 1, use = local >> 1;
+        if (!mbar_wait(&tempty_bar[acc], (use & 1) ^ 1)) {
+          report_error(args.err, kErrGemmWaitTimeout, 2);
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES, r = it / STAGES;
+          if (!mbar_wait(&full_bar[s], r & 1)) {
+            report_error(args.err, kErrGemmWaitTimeout, 3);
+            return false;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * A_STAGE_BYTES);
+          const uint32_t b_base = smem_u32(sB + s * B_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a_base + k * 2048, 8192, 1024)
+                                        : umma_desc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? umma_desc_sw128(b_base + k * 2048, 8192, 1024)
+                                        : umma_desc_sw128(b_base + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[s]);  // frees the smem stage when these UMMAs finish
+        }
+        umma_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
+        ++local;
+        return true;
+      });
+      // Make sure every UMMA this thread issued has completed before TMEM is released.
+      umma_commit(drain_bar);
+      mbar_wait(drain_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int local = 0;
+    for_each_segment(sched, stream_k, [&](int tile, int kb0, int kb1) -> bool {
+      const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
+      const int acc = local & 1, use = local >> 1;
+      if (!mbar_wait(&tfull_bar[acc], use & 1)) {
+        report_error(args.err, kErrGemmWaitTimeout, 4);
+        return false;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const int m = mt * BM + row;
+      const bool row_ok = m < args.M;
+
+      if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_load_f32x32(taddr + c * 32, v);
+          const int n = nt * BN + c * 32;
+          if (row_ok && n < args.N) {
+            if constexpr (EPI == EPI_RESIDUAL) {
+              float rsd[32];
+              load_bf16x32(args.residual + (long)m * args.ldr + n, rsd);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += rsd[j];
+            }
+            store_bf16x32(out + (long)m * args.ldo + n, v);
+          }
+        }
+      } else if constexpr (EPI == EPI_F32ADD) {
+        float* out = reinterpret_cast<float*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_load_f32x32(taddr + c * 32, v);
+          const int n = nt * BN + c * 32;
+          if (row_ok && n < args.N) {
+            float4* dst = reinterpret_cast<float4*>(out + (long)m * args.ldo + n);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              atomicAdd(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+          }
+        }
+      } else if constexpr (EPI == EPI_ROPE) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+        const int pos = row_ok ? args.positions[m] : 0;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {  // two 128-wide heads per tile
+          const int head_col = nt * BN + h * 128;
+          const bool rotate = head_col >= args.rope_begin && head_col < args.rope_end;
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {  // columns [c*32, c*32+32) pair with +64
+            float x1[32], x2[32];
+            tmem_load_f32x32(taddr + h * 128 + c * 32, x1);
+            tmem_load_f32x32(taddr + h * 128 + 64 + c * 32, x2);
+            if (row_ok && head_col < args.N) {
+              if (rotate) {
+                const float* cr = args.cos_tab + (long)pos * 64 + c * 32;
+                const float* sr = args.sin_tab + (long)pos * 64 + c * 32;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const float cs = cr[j], sn = sr[j];
+                  const float a = x1[j], b = x2[j];
+                  x1[j] = a * cs - b * sn;
+                  x2[j] = b * cs + a * sn;
+                }
+              }
+              store_bf16x32(out + (long)m * args.ldo + head_col + c * 32, x1);
+              store_bf16x32(out + (long)m * args.ldo + head_col + 64 + c * 32, x2);
+            }
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
+        // acc columns [0,128) = gate, [128,256) = up for features nt*128 + [0,128)
+        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(args.out);
+        __nv_bfloat16* hout = reinterpret_cast<__nv_bfloat16*>(args.out2);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float g[32], u[32];
+          tmem_load_f32x32(taddr + c * 32, g);
+          tmem_load_f32x32(taddr + 128 + c * 32, u);
+          const int f = nt * 128 + c * 32;
+          if (row_ok && f < args.N) {
+            float hv[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              g[j] = bf16_round(g[j]);
+              u[j] = bf16_round(u[j]);
+              hv[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+            }
+            store_bf16x32(gu + (long)m * args.ldo + f, g);
+            store_bf16x32(gu + (long)m * args.ldo + args.pair_offset + f, u);
+            store_bf16x32(hout + (long)m * args.ldo2 + f, hv);
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+        __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float dh[32];
+          tmem_load_f32x32(taddr + c * 32, dh);
+          const int f = nt * BN + c * 32;
+          if (row_ok && f < args.N) {
+            float g[32], u[32];
+            load_bf16x32(args.aux + (long)m * args.ldaux + f, g);
+            load_bf16x32(args.aux + (long)m * args.ldaux + args.pair_offset + f, u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float sg = 1.0f / (1.0f + __expf(-g[j]));
+              const float silu = g[j] * sg;
+              const float dsilu = sg * (1.0f + g[j] * (1.0f - sg));
+              const float d = bf16_round(dh[j]);
+              g[j] = d * u[j] * dsilu;
+              u[j] = d * silu;
+            }
+            store_bf16x32(dgu + (long)m * args.ldo + f, g);
+            store_bf16x32(dgu + (long)m * args.ldo + args.pair_offset + f, u);
+          }
+        }
+      } else if constexpr (EPI == EPI_CE) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+        const int label = row_ok ? args.labels[m] : -1;
+        float run_max = -INFINITY, run_sum = 0.0f;
+        int run_arg = 0;
+        constexpr float kLog2e = 1.4426950408889634f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_load_f32x32(taddr + c * 32, v);
+          const int n = nt * BN + c * 32;
+          if (row_ok && n < args.N) {
+            float cmax = -INFINITY;
+            int carg = 0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] = bf16_round(v[j]);
+              if (v[j] > cmax) {
+                cmax = v[j];
+                carg = j;
+              }
+              if (n + j == label) args.ce_tgt[m] = v[j];
+            }
+            const float new_max = fmaxf(run_max, cmax);
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) s += fast_exp2((v[j] - new_max) * kLog2e);
+            run_sum = run_sum * fast_exp2((run_max - new_max) * kLog2e) + s;
+            if (cmax > run_max) run_arg = n + carg;
+            run_max = new_max;
+            store_bf16x32(out + (long)m * args.ldo + n, v);
+          }
+        }
+        if (row_ok) {
+          const long idx = (long)nt * args.M + m;
+          args.ce_max[idx] = run_max;
+          args.ce_sum[idx] = run_sum;
+          args.ce_arg[idx] = run_arg;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      ++local;
+      return true;
+    });
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    TORCH_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+                    ptr != nullptr,
+                "cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2D bf16 tensor map over a row-major matrix [outer, inner] with row stride `ld` elements.
+CUtensorMap make_map(const at::Tensor& t, int64_t inner, int64_t outer, int64_t ld, uint32_t box_inner,
+                     uint32_t box_outer) {
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, "GEMM operands must be bf16");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, "GEMM operand base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "GEMM operand row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  return map;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int A_MN, int B_MN, int EPI>
+void launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int grid, cudaStream_t stream) {
+  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM_BYTES) ==
+                    cudaSuccess,
+                "cudaFuncSetAttribute failed");
+    configured = true;
+  }
+  kern<<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, stream>>>(ma, mb, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+at::Tensor device_error_word();  // errors.cu
+
+// Generic entry: see the file header for operand conventions.
+//   a: [M,K] (a_mn=0) or [K,M] (a_mn=1);  b: [Nb,K] (b_mn=0) or [K,N] (b_mn=1)
+void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_t M, int64_t N, int64_t K,
+          int64_t epi, const at::Tensor& out, const c10::optional<at::Tensor>& out2,
+          const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& aux,
+          const c10::optional<at::Tensor>& positions, const c10::optional<at::Tensor>& cos_tab,
+          const c10::optional<at::Tensor>& sin_tab, int64_t rope_begin, int64_t rope_end, int64_t pair_offset,
+          const c10::optional<at::Tensor>& labels, const c10::optional<at::Tensor>& ce_max,
+          const c10::optional<at::Tensor>& ce_sum, const c10::optional<at::Tensor>& ce_arg,
+          const c10::optional<at::Tensor>& ce_tgt, bool stream_k) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm: row-major 2D operands");
+  TORCH_CHECK(N % 32 == 0, "gemm: N must be a multiple of 32");
+  c10::cuda::CUDAGuard guard(a.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.out = out.data_ptr();
+  args.ldo = out.stride(0);
+  TORCH_CHECK(out.stride(1) == 1 && out.stride(0) % 8 == 0, "gemm: output rows must be contiguous and 16B aligned");
+  if (out2) { args.out2 = out2->data_ptr(); args.ldo2 = out2->stride(0); }
+  if (residual) { args.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()); args.ldr = residual->stride(0); }
+  if (aux) { args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr()); args.ldaux = aux->stride(0); }
+  if (positions) args.positions = positions->data_ptr<int>();
+  if (cos_tab) args.cos_tab = cos_tab->data_ptr<float>();
+  if (sin_tab) args.sin_tab = sin_tab->data_ptr<float>();
+  args.rope_begin = (int)rope_begin;
+  args.rope_end = (int)rope_end;
+  args.pair_offset = (int)pair_offset;
+  if (labels) args.labels = labels->data_ptr<int>();
+  if (ce_max) args.ce_max = ce_max->data_ptr<float>();
+  if (ce_sum) args.ce_sum = ce_sum->data_ptr<float>();
+  if (ce_arg) args.ce_arg = ce_arg->data_ptr<int>();
+  if (ce_tgt) args.ce_tgt = ce_tgt->data_ptr<float>();
+  args.err = device_error_word().data_ptr<int>();
+  args.stream_k = stream_k ? 1 : 0;
+
+  CUtensorMap ma = a_mn ? make_map(a, M, K, a.stride(0), 64, 64) : make_map(a, K, M, a.stride(0), 64, 128);
+  const int64_t b_rows = b_mn ? K : b.size(0);
+  CUtensorMap mb = b_mn ? make_map(b, N, K, b.stride(0), 64, 64) : make_map(b, K, b_rows, b.stride(0), 64, 128);
+
+  const int64_t m_tiles = (M + BM - 1) / BM;
+  const int64_t n_tiles = (epi == EPI_SWIGLU) ? (N + 127) / 128 : (N + BN - 1) / BN;
+  const int64_t tiles = m_tiles * n_tiles;
+  int grid = (int)std::min<int64_t>(tiles, num_sms());
+  if (epi == EPI_F32ADD && stream_k) grid = num_sms();
+
+#define HRM_GEMM_CASE(AM, BMJ, E) \
+  if (a_mn == AM && b_mn == BMJ && epi == E) return launch<AM, BMJ, E>(ma, mb, args, grid, stream);
+  HRM_GEMM_CASE(0, 0, EPI_STORE)
+  HRM_GEMM_CASE(0, 0, EPI_RESIDUAL)
+  HRM_GEMM_CASE(0, 0, EPI_ROPE)
+  HRM_GEMM_CASE(0, 0, EPI_SWIGLU)
+  HRM_GEMM_CASE(0, 0, EPI_CE)
+  HRM_GEMM_CASE(0, 0, EPI_F32ADD)
+  HRM_GEMM_CASE(0, 1, EPI_STORE)
+  HRM_GEMM_CASE(0, 1, EPI_RESIDUAL)
+  HRM_GEMM_CASE(0, 1, EPI_SWIGLU_BWD)
+  HRM_GEMM_CASE(1, 1, EPI_F32ADD)
+  HRM_GEMM_CASE(1, 1, EPI_STORE)
+#undef HRM_GEMM_CASE
+  TORCH_CHECK(false, "gemm: unsupported (a_mn, b_mn, epilogue) combination ", a_mn, b_mn, epi);
+}
+
+}  // namespace hrm

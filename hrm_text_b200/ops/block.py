@@ -1,0 +1,140 @@
+"""Fused transformer layer on sm_100a kernels (one autograd node per layer).
+
+Forward of a pre-norm layer (reference models/transformer.py:90-92, models/layers.py:129-168):
+
+    s   = x (+ injection)                      fused into the first RMSNorm
+    xn  = rmsnorm(s)
+    g|q|k|v = xn @ Wgqkv^T, RoPE on q, k       GEMM with RoPE epilogue
+    O, Y = attention(q, k, v), Y = sigmoid(g) * O   flash attention, gate in the epilogue
+    x1  = s + Y @ Wo^T                         GEMM with residual epilogue
+    xn2 = rmsnorm(x1)
+    gu, h = xn2 @ Wgu^T, h = silu(gate) * up   GEMM with SwiGLU epilogue
+    x2  = x1 + h @ Wd^T                        GEMM with residual epilogue
+
+The backward is written out by hand (no autograd inside): dgrad GEMMs with fused SwiGLU /
+residual epilogues, fp32 weight-gradient GEMMs accumulating straight into each weight's
+``main_grad`` buffer (so the gradients of the 2-3 recurrent calls that reuse a layer add
+up in fp32 without extra passes), and the flash-attention backward with the gate and RoPE
+backward fused. Weight tensors are the bf16 compute copies; when a weight has no
+``main_grad`` the node returns an ordinary gradient instead.
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from .._native import cuda
+from . import gemm as G
+from .attention import PackedSeq, attention_bwd, attention_fwd, rope_half_tables
+
+
+def rmsnorm(x: Tensor, eps: float, injection: Tensor | None = None):
+    """Returns ``(y, rstd, s)``; ``s = bf16(x + injection)`` when an injection is given (else ``x``)."""
+    T, H = (injection.shape if injection is not None else x.shape)
+    y = torch.empty((T, H), dtype=torch.bfloat16, device=(injection if injection is not None else x).device)
+    rstd = torch.empty((T,), dtype=torch.float32, device=y.device)
+    if injection is not None:
+        s = torch.empty_like(y)
+        cuda().rmsnorm_fwd(x, injection, s, y, rstd, T, eps)
+    else:
+        cuda().rmsnorm_fwd(x, None, None, y, rstd, T, eps)
+        s = x
+    return y, rstd, s
+
+
+def rmsnorm_bwd(dy: Tensor, s: Tensor, rstd: Tensor, dres: Tensor | None = None) -> Tensor:
+    dx = torch.empty_like(dy)
+    cuda().rmsnorm_bwd(dy, s, rstd, dres, dx, dy.shape[0])
+    return dx
+
+
+def _wgrad(dy: Tensor, x: Tensor, w: Tensor, grads: list, idx: int) -> None:
+    main = getattr(w, "main_grad", None)
+    if main is not None:
+        G.linear_wgrad_(dy, x, main)
+    else:
+        g = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        G.linear_wgrad_(dy, x, g)
+        grads[idx] = g.to(w.dtype)
+
+
+class FusedPreNormBlock(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, injection, w_gqkv, w_o, w_gu, w_d, packed: PackedSeq, rope, num_heads: int, eps: float,
+                causal: bool, train: bool):
+        cos, sin = rope
+        hidden = w_o.shape[0]
+        xn, r1, s = rmsnorm(x, eps, injection)
+        sched = packed.schedule(causal)
+        gqkv = G.linear_rope(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden)
+        o, y, lse = attention_fwd(gqkv, num_heads, sched)
+        x1 = G.linear(y, w_o, residual=s)
+        xn2, r2, _ = rmsnorm(x1, eps)
+        gu, h = G.linear_swiglu(xn2, w_gu)
+        x2 = G.linear(h, w_d, residual=x1)
+        if train:
+            ctx.save_for_backward(s, r1, xn, gqkv, o, lse, y, x1, r2, xn2, gu, h, w_gqkv, w_o, w_gu, w_d, cos, sin)
+            ctx.packed, ctx.num_heads, ctx.causal = packed, num_heads, causal
+            ctx.has_injection = injection is not None
+        return x2
+
+    @staticmethod
+    def backward(ctx, dx2):
+        (s, r1, xn, gqkv, o, lse, y, x1, r2, xn2, gu, h, w_gqkv, w_o, w_gu, w_d, cos, sin) = ctx.saved_tensors
+        packed = ctx.packed
+        dx2 = dx2.contiguous()
+        grads = [None] * 4
+        # MLP
+        dgu = G.linear_dgrad_swiglu(dx2, w_d, gu)
+        _wgrad(dx2, h, w_d, grads, 3)
+        dxn2 = G.linear_dgrad(dgu, w_gu)
+        _wgrad(dgu, xn2, w_gu, grads, 2)
+        dx1 = rmsnorm_bwd(dxn2, x1, r2, dres=dx2)
+        # attention
+        dy = G.linear_dgrad(dx1, w_o)
+        _wgrad(dx1, y, w_o, grads, 1)
+        dgqkv = attention_bwd(gqkv, ctx.num_heads, packed.schedule(ctx.causal), o, lse, dy, packed.position_ids,
+                              cos, sin)
+        dxn = G.linear_dgrad(dgqkv, w_gqkv)
+        _wgrad(dgqkv, xn, w_gqkv, grads, 0)
+        ds = rmsnorm_bwd(dxn, s, r1, dres=dx1)
+        d_inj = ds if ctx.has_injection else None
+        return (ds, d_inj, grads[0], grads[1], grads[2], grads[3], None, None, None, None, None, None)
+
+
+class FinalNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, eps: float):
+        y, rstd, _ = rmsnorm(x, eps)
+        ctx.save_for_backward(x, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, rstd = ctx.saved_tensors
+        return rmsnorm_bwd(dy.contiguous(), x, rstd), None
+
+
+def stack_forward(stack, x: Tensor, injection: Tensor | None, seq_info: dict) -> Tensor:
+    """Run ``hrm_text_b200.models.transformer.Transformer`` on the fused CUDA path."""
+    cfg = stack.config
+    if cfg.norm_type != "pre":
+        raise NotImplementedError("the fused CUDA block implements pre-norm layers (all shipped sizes)")
+    if cfg.head_dim != 128:
+        raise NotImplementedError("the fused CUDA block is specialised for head_dim 128")
+    if not hasattr(stack, "rotary_emb"):
+        raise NotImplementedError("the fused CUDA block applies RoPE (pos_emb_type 'rope')")
+    packed = PackedSeq.from_seq_info(seq_info)
+    rope = rope_half_tables(stack.rotary_emb)
+    causal = cfg.attn_type == "causal"
+    train = torch.is_grad_enabled()
+    if injection is not None and x.dim() == 1:  # broadcast initial state (zL_init)
+        x = x.to(injection.dtype).expand_as(injection)
+    if x.dim() == 2 and x.stride(0) == 0:
+        x = x.contiguous()
+    for i, layer in enumerate(stack.layers):
+        a, m = layer.attn, layer.mlp
+        x = FusedPreNormBlock.apply(x, injection if i == 0 else None, a.gqkv_proj.weight, a.o_proj.weight,
+                                    m.gate_up_proj.weight, m.down_proj.weight, packed, rope, a.num_heads,
+                                    cfg.norm_eps, causal, train)
+    return FinalNorm.apply(x, cfg.norm_eps)

@@ -1,0 +1,112 @@
+"""Python entry points of the tcgen05 GEMM (csrc/kernels/gemm_tcgen05.cu).
+
+Conventions (row-major tensors, bf16 operands):
+
+* ``linear(x, w)``                 ``y = x @ w.T``            x [M,K], w [N,K]
+* ``linear_dgrad(dy, w)``          ``dx = dy @ w``            dy [M,N], w [N,K]
+* ``linear_wgrad_(dy, x, grad)``   ``grad += dy.T @ x`` (fp32, stream-K split with atomics)
+
+plus the fused-epilogue variants used by the transformer block and the LM head.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from .._native import cuda
+
+EPI_STORE, EPI_RESIDUAL, EPI_F32ADD, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_CE = range(7)
+
+
+def _check(*tensors: Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError("hrm_text_b200.ops.gemm takes CUDA tensors only")
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError(f"GEMM operands must be bf16, got {t.dtype}")
+
+
+def _gemm(a, a_mn, b, b_mn, M, N, K, epi, out, out2=None, residual=None, aux=None, positions=None, cos=None,
+          sin=None, rope_begin=0, rope_end=0, pair_offset=0, labels=None, ce_max=None, ce_sum=None, ce_arg=None,
+          ce_tgt=None, stream_k=False):
+    cuda().gemm(a, a_mn, b, b_mn, M, N, K, epi, out, out2, residual, aux, positions, cos, sin, rope_begin, rope_end,
+                pair_offset, labels, ce_max, ce_sum, ce_arg, ce_tgt, stream_k)
+
+
+def linear(x: Tensor, w: Tensor, out: Optional[Tensor] = None, residual: Optional[Tensor] = None) -> Tensor:
+    _check(x, w)
+    M, K = x.shape
+    N = w.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device) if out is None else out
+    _gemm(x, False, w, False, M, N, K, EPI_RESIDUAL if residual is not None else EPI_STORE, out, residual=residual)
+    return out
+
+
+def linear_rope(x: Tensor, w: Tensor, positions: Tensor, cos: Tensor, sin: Tensor, rope_begin: int,
+                rope_end: int) -> Tensor:
+    """``x @ w.T`` with rotate-half RoPE (head_dim 128) on output columns [rope_begin, rope_end)."""
+    _check(x, w)
+    M, K = x.shape
+    N = w.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _gemm(x, False, w, False, M, N, K, EPI_ROPE, out, positions=positions, cos=cos, sin=sin, rope_begin=rope_begin,
+          rope_end=rope_end)
+    return out
+
+
+def linear_swiglu(x: Tensor, w: Tensor) -> tuple[Tensor, Tensor]:
+    """For ``w = [gate; up]`` (``[2I, K]``): returns ``(gate|up [M, 2I], silu(gate) * up [M, I])``."""
+    _check(x, w)
+    M, K = x.shape
+    inter = w.shape[0] // 2
+    gu = torch.empty((M, 2 * inter), dtype=torch.bfloat16, device=x.device)
+    h = torch.empty((M, inter), dtype=torch.bfloat16, device=x.device)
+    _gemm(x, False, w, False, M, inter, K, EPI_SWIGLU, gu, out2=h, pair_offset=inter)
+    return gu, h
+
+
+def linear_dgrad(dy: Tensor, w: Tensor, out: Optional[Tensor] = None, residual: Optional[Tensor] = None) -> Tensor:
+    _check(dy, w)
+    M, N = dy.shape
+    K = w.shape[1]
+    out = torch.empty((M, K), dtype=torch.bfloat16, device=dy.device) if out is None else out
+    _gemm(dy, False, w, True, M, K, N, EPI_RESIDUAL if residual is not None else EPI_STORE, out, residual=residual)
+    return out
+
+
+def linear_dgrad_swiglu(dy: Tensor, w_down: Tensor, gu: Tensor) -> Tensor:
+    """``dh = dy @ w_down`` followed by the SwiGLU backward: returns ``d(gate|up) [M, 2I]``."""
+    _check(dy, w_down, gu)
+    M, N = dy.shape
+    inter = w_down.shape[1]
+    dgu = torch.empty((M, 2 * inter), dtype=torch.bfloat16, device=dy.device)
+    _gemm(dy, False, w_down, True, M, inter, N, EPI_SWIGLU_BWD, dgu, aux=gu, pair_offset=inter)
+    return dgu
+
+
+def linear_wgrad_(dy: Tensor, x: Tensor, grad: Tensor) -> Tensor:
+    """``grad += dy.T @ x`` in fp32 (``grad`` is ``[N, K]`` fp32, contiguous)."""
+    _check(dy, x)
+    assert grad.dtype == torch.float32 and grad.is_contiguous()
+    T, N = dy.shape
+    K = x.shape[1]
+    _gemm(dy, True, x, True, N, K, T, EPI_F32ADD, grad, stream_k=True)
+    return grad
+
+
+def lm_head_ce_logits(x: Tensor, w: Tensor, labels: Tensor):
+    """Logits ``x @ w.T`` (bf16) plus per-256-column partial softmax statistics."""
+    _check(x, w)
+    M, K = x.shape
+    V = w.shape[0]
+    n_tiles = (V + 255) // 256
+    logits = torch.empty((M, V), dtype=torch.bfloat16, device=x.device)
+    pmax = torch.empty((n_tiles, M), dtype=torch.float32, device=x.device)
+    psum = torch.empty((n_tiles, M), dtype=torch.float32, device=x.device)
+    parg = torch.empty((n_tiles, M), dtype=torch.int32, device=x.device)
+    tgt = torch.zeros((M,), dtype=torch.float32, device=x.device)
+    _gemm(x, False, w, False, M, V, K, EPI_CE, logits, labels=labels, ce_max=pmax, ce_sum=psum, ce_arg=parg,
+          ce_tgt=tgt)
+    return logits, pmax, psum, parg, tgt

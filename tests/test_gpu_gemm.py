@@ -1,0 +1,95 @@
+"""tcgen05 GEMM and its fused epilogues vs fp32 torch references."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from gpu_utils import assert_close
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(256, 256, 128), (300, 512, 192), (1000, 1280, 1280), (128, 768, 64)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_linear_fwd(cuda_device, M, N, K):
+    from hrm_text_b200.ops import gemm as G
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device=cuda_device).bfloat16()
+    w = torch.randn(N, K, device=cuda_device).bfloat16()
+    ref = x.float() @ w.float().T
+    assert_close(G.linear(x, w), ref, 1e-2, "fwd")
+    r = torch.randn(M, N, device=cuda_device).bfloat16()
+    assert_close(G.linear(x, w, residual=r), ref + r.float(), 1e-2, "fwd+residual")
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_linear_dgrad_wgrad(cuda_device, M, N, K):
+    from hrm_text_b200.ops import gemm as G
+    torch.manual_seed(1)
+    dy = torch.randn(M, N, device=cuda_device).bfloat16()
+    w = torch.randn(N, K, device=cuda_device).bfloat16()
+    x = torch.randn(M, K, device=cuda_device).bfloat16()
+    assert_close(G.linear_dgrad(dy, w), dy.float() @ w.float(), 1e-2, "dgrad")
+    grad = torch.full((N, K), 0.5, device=cuda_device)
+    G.linear_wgrad_(dy, x, grad)
+    assert_close(grad, 0.5 + dy.float().T @ x.float(), 1e-3, "wgrad accumulate")
+
+
+def test_linear_rope(cuda_device):
+    from hrm_text_b200.models.layers import apply_rotary_pos_emb, rope_tables
+    from hrm_text_b200.ops import gemm as G
+    torch.manual_seed(2)
+    M, H, K = 384, 2, 256
+    N = 4 * H * 128
+    x = torch.randn(M, K, device=cuda_device).bfloat16()
+    w = torch.randn(N, K, device=cuda_device).bfloat16()
+    pos = torch.randint(0, 1000, (M,), device=cuda_device, dtype=torch.int32)
+    cos, sin = rope_tables(128, 1024, 10000.0, device=cuda_device)
+    out = G.linear_rope(x, w, pos, cos[:, :64].contiguous(), sin[:, :64].contiguous(), H * 128, 3 * H * 128)
+    ref = (x.float() @ w.float().T).view(M, 4 * H, 128)
+    cs = (cos[pos.long()], sin[pos.long()])
+    ref[:, H:3 * H] = apply_rotary_pos_emb(ref[:, H:3 * H], cs)
+    assert_close(out, ref.view(M, N), 1e-2, "rope epilogue")
+
+
+def test_linear_swiglu_fwd_bwd(cuda_device):
+    from hrm_text_b200.ops import gemm as G
+    torch.manual_seed(3)
+    M, K, I = 300, 256, 384
+    x = torch.randn(M, K, device=cuda_device).bfloat16()
+    w = (torch.randn(2 * I, K, device=cuda_device) / 16).bfloat16()
+    gu, h = G.linear_swiglu(x, w)
+    gu_ref = x.float() @ w.float().T
+    assert_close(gu, gu_ref, 1e-2, "gate|up")
+    g, u = gu_ref.bfloat16().float().chunk(2, -1)
+    assert_close(h, F.silu(g) * u, 2e-2, "silu*up")
+    wd = torch.randn(512, I, device=cuda_device).bfloat16()
+    dy = torch.randn(M, 512, device=cuda_device).bfloat16()
+    dgu = G.linear_dgrad_swiglu(dy, wd, gu)
+    gr = g.clone().requires_grad_(True)
+    ur = u.clone().requires_grad_(True)
+    (F.silu(gr) * ur).backward((dy.float() @ wd.float()).bfloat16().float())
+    assert_close(dgu, torch.cat([gr.grad, ur.grad], -1), 2e-2, "swiglu bwd")
+
+
+def test_lm_head_cross_entropy(cuda_device):
+    from hrm_text_b200.ops.loss import lm_head_cross_entropy
+    torch.manual_seed(4)
+    T, H, V = 500, 256, 2048
+    x = torch.randn(T, H, device=cuda_device).bfloat16().requires_grad_(True)
+    w = (torch.randn(V, H, device=cuda_device) / 16).bfloat16().requires_grad_(True)
+    labels = torch.randint(0, V, (T,), device=cuda_device, dtype=torch.int32)
+    labels[::7] = -100
+    loss, correct = lm_head_cross_entropy(x, w, labels)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    logits = (xr @ wr.T).bfloat16().float()
+    ref = F.cross_entropy(logits, labels.long(), ignore_index=-100, reduction="sum")
+    assert abs(loss.item() - ref.item()) <= 2e-3 * abs(ref.item())
+    valid = labels >= 0
+    ref_correct = (logits.argmax(-1) == labels.long()) & valid
+    assert (correct == ref_correct).float().mean().item() > 0.995
+    (loss * 0.01).backward()
+    (ref * 0.01).backward()
+    assert_close(x.grad, xr.grad, 3e-2, "d hidden")
+    assert_close(w.grad, wr.grad, 3e-2, "d weight")
