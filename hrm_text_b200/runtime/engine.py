@@ -313,27 +313,28 @@ class GraphedTrainStep:
         for k in BATCH_KEYS:
             self.static[k].copy_(batch[k], non_blocking=True)
 
-    def _capture(self, bp_steps: int) -> None:
+    def capture(self, key, extra: dict) -> None:
+        """Warm up eagerly (side stream), then capture one step body for ``extra`` kwargs."""
         eng = self.engine
-        # eager warm-up on a side stream (first launches configure kernels / allocate)
         self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
             for _ in range(self.warmup):
-                eng.params.zero_grad()
-                eng.forward_backward(self.static, bp_steps=bp_steps)
+                eng.forward_backward(self.static, **extra)
         torch.cuda.current_stream().wait_stream(self.stream)
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()  # release warm-up activations before the graph pool grows
         eng.params.zero_grad()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, pool=self.pool, stream=self.stream):
-            out = eng.step_body(self.static, bp_steps=bp_steps)
+            out = eng.step_body(self.static, **extra)
         self.pool = g.pool()
-        self.graphs[bp_steps] = g
-        self.outputs[bp_steps] = out
+        self.graphs[key] = g
+        self.outputs[key] = out
 
     def __call__(self, batch: dict, lr: float, bp_steps: int):
         self.load(batch)
         if bp_steps not in self.graphs:
-            self._capture(bp_steps)  # warm-up runs forward/backward only; capture executes nothing
+            self.capture(bp_steps, {"bp_steps": bp_steps})  # warm-up runs forward/backward only
         self.engine.params.set_hyper(lr)
         self.graphs[bp_steps].replay()
         return self.outputs[bp_steps]
