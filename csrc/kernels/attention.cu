@@ -825,3 +825,85 @@ void attn_bwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const a
 }
 
 }  // namespace hrm
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free attention forward (declared in attention_noalloc.h; no counterpart in
+// the reference). Same kernels as attn_fwd above; the schedule scratch is the static
+// device array below instead of a caller-provided tensor.
+// ---------------------------------------------------------------------------------------
+#include "attention_noalloc.h"
+
+namespace hrm {
+namespace attn {
+// Work schedule + counters for hrm_attn_fwd_noalloc, one per GPU that loads the library.
+static __device__ __align__(256) int g_noalloc_sched[HRM_ATTN_NOALLOC_SCRATCH_BYTES / 4];
+}  // namespace attn
+}  // namespace hrm
+
+namespace {
+constexpr int kMaxDevices = 64;
+int* g_noalloc_ptr[kMaxDevices] = {};
+int g_noalloc_sms[kMaxDevices] = {};
+
+// Once per device, with that device current: resolve the static array's device address
+// (host code must not use the symbol itself) and configure the kernel.
+cudaError_t noalloc_setup(int dev) {
+  if (g_noalloc_ptr[dev] != nullptr) return cudaSuccess;
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, hrm::attn::g_noalloc_sched);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(hrm::attn::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           hrm::attn::FWD_SMEM);
+  if (e != cudaSuccess) return e;
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  g_noalloc_sms[dev] = sms;
+  g_noalloc_ptr[dev] = static_cast<int*>(ptr);
+  return cudaSuccess;
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) const char* hrm_attn_fwd_noalloc_strerror(int code) {
+  if (code == 0) return "success";
+  if (code == HRM_ATTN_NOALLOC_TOO_LARGE)
+    return "problem too large for the static scratch: need ceil(T/128) + n_cu <= HRM_ATTN_NOALLOC_MAX_TILES";
+  if (code == HRM_ATTN_NOALLOC_BAD_ARG) return "invalid argument (null pointer, head count or row stride)";
+  return cudaGetErrorString(static_cast<cudaError_t>(code));
+}
+
+extern "C" __attribute__((visibility("default"))) int hrm_attn_fwd_noalloc(
+    const void* qkv, long long ld_qkv, int T, int num_heads, const int* cu_seqlens, int n_cu, const int* prefix_lens,
+    int causal, void* out, void* y, long long ld_out, float* lse, cudaStream_t stream) {
+  if (qkv == nullptr || cu_seqlens == nullptr || prefix_lens == nullptr || out == nullptr || y == nullptr ||
+      lse == nullptr || T <= 0 || num_heads <= 0 || n_cu < 1 || ld_qkv < 4LL * num_heads * hrm::attn::D ||
+      ld_out < (long long)num_heads * hrm::attn::D || (ld_qkv % 8) != 0 || (ld_out % 8) != 0)
+    return HRM_ATTN_NOALLOC_BAD_ARG;
+  const long long tiles = (T + 127) / 128 + (long long)n_cu;
+  if (tiles > HRM_ATTN_NOALLOC_MAX_TILES) return HRM_ATTN_NOALLOC_TOO_LARGE;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev >= kMaxDevices) return HRM_ATTN_NOALLOC_BAD_ARG;
+  e = noalloc_setup(dev);
+  if (e != cudaSuccess) return (int)e;
+  int* sched = g_noalloc_ptr[dev];
+  const int cap = HRM_ATTN_NOALLOC_MAX_TILES;
+
+  hrm::attn::schedule_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, prefix_lens, n_cu, causal ? 1 : 0, cap, sched);
+  hrm::attn::FwdParams p{};
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.ld_qkv = ld_qkv;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ld_out = ld_out;
+  p.lse = lse;
+  p.T = T;
+  p.H = num_heads;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hrm::attn::D));
+  p.sched = sched;
+  p.cap = cap;
+  hrm::attn::attn_fwd_kernel<<<g_noalloc_sms[dev], hrm::attn::FWD_THREADS, hrm::attn::FWD_SMEM, stream>>>(p);
+  hrm::attn::attn_zero_tail_kernel<<<64, 256, 0, stream>>>(p.out, p.y, p.ld_out, p.lse, p.T, p.H, p.sched);
+  return (int)cudaGetLastError();
+}
