@@ -9,10 +9,11 @@
 //   wgrad    dW = dY^T X : A = dY [T,N] MN-major, B = X [T,K]  MN-major
 //
 // CTA tile 128 x 256 x 64, 4-stage TMA ring (48 KB / stage, 128B swizzle), one CTA per SM.
-// Warp roles (192 threads):
+// Warp roles (320 threads):
 //   warp 0      : TMA producer (one elected lane)
 //   warp 1      : TMEM allocator + UMMA issuer (one elected lane)
-//   warps 2..5  : epilogue; TMEM lane quarter = warp % 4, one accumulator row per thread
+//   warps 2..9  : epilogue; TMEM lane quarter = warp % 4, one accumulator row per thread;
+//                 warps 2-5 and 6-9 split the tile's columns (two warps per lane quarter)
 // The accumulator is double-buffered in TMEM (2 x 256 columns), so the epilogue of tile i
 // overlaps the main loop of tile i+1.
 //
@@ -27,7 +28,8 @@
 //   ROPE      out bf16 = acc, with rotate-half RoPE on the q/k head columns
 //   SWIGLU    B rows are gate/up pairs; writes gate|up and silu(gate)*up
 //   SWIGLU_BWD acc = dh; reads gate|up, writes d(gate)|d(up)
-//   CE        out bf16 logits + per-row partial (max, sum exp, argmax, target logit)
+//   CE        out bf16 logits + per-row partial (max, sum exp, argmax, target logit) per
+//             128-column half tile
 //
 // All mbarrier waits are bounded (common.cuh); on a timeout the kernel records an error,
 // drains its own TMA loads and UMMAs, frees TMEM and returns.
@@ -52,7 +54,8 @@ enum GemmEpilogue : int {
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
-constexpr int GEMM_THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int GEMM_SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256;
 
@@ -75,7 +78,7 @@ struct GemmArgs {
   int pair_offset;
   // cross-entropy partials, [n_tiles, M]
   const int* labels;
-  float* ce_max;
+  float* ce_max;  // [2 * n_tiles, M]
   float* ce_sum;
   int* ce_arg;
   float* ce_tgt;
@@ -178,7 +181,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 32 * EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
@@ -289,6 +292,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // which column half of the tile this warp handles
     const int row = quarter * 32 + lane;
     int local = 0;
     for_each_segment(sched, stream_k, [&](int tile, int kb0, int kb1) -> bool {
@@ -306,7 +310,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * 4; c < half * 4 + 4; ++c) {
           float v[32];
           tmem_load_f32x32(taddr + c * 32, v);
           const int n = nt * BN + c * 32;
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       } else if constexpr (EPI == EPI_F32ADD) {
         float* out = reinterpret_cast<float*>(args.out);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * 4; c < half * 4 + 4; ++c) {
           float v[32];
           tmem_load_f32x32(taddr + c * 32, v);
           const int n = nt * BN + c * 32;
@@ -335,32 +339,40 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       } else if constexpr (EPI == EPI_ROPE) {
+        // This warp handles frequency chunk c = half (columns [c*32, c*32+32) paired with +64)
+        // of both 128-wide heads of the tile; the cos/sin row slice is loaded once.
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+        const int c = half;
         const int pos = row_ok ? args.positions[m] : 0;
+        float cs[32], sn[32];
+        {
+          const float4* cr = reinterpret_cast<const float4*>(args.cos_tab + (long)pos * 64 + c * 32);
+          const float4* sr = reinterpret_cast<const float4*>(args.sin_tab + (long)pos * 64 + c * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 a = cr[q], b = sr[q];
+            cs[4 * q] = a.x; cs[4 * q + 1] = a.y; cs[4 * q + 2] = a.z; cs[4 * q + 3] = a.w;
+            sn[4 * q] = b.x; sn[4 * q + 1] = b.y; sn[4 * q + 2] = b.z; sn[4 * q + 3] = b.w;
+          }
+        }
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {  // two 128-wide heads per tile
+        for (int h = 0; h < 2; ++h) {
           const int head_col = nt * BN + h * 128;
           const bool rotate = head_col >= args.rope_begin && head_col < args.rope_end;
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {  // columns [c*32, c*32+32) pair with +64
-            float x1[32], x2[32];
-            tmem_load_f32x32(taddr + h * 128 + c * 32, x1);
-            tmem_load_f32x32(taddr + h * 128 + 64 + c * 32, x2);
-            if (row_ok && head_col < args.N) {
-              if (rotate) {
-                const float* cr = args.cos_tab + (long)pos * 64 + c * 32;
-                const float* sr = args.sin_tab + (long)pos * 64 + c * 32;
+          float x1[32], x2[32];
+          tmem_load_f32x32(taddr + h * 128 + c * 32, x1);
+          tmem_load_f32x32(taddr + h * 128 + 64 + c * 32, x2);
+          if (row_ok && head_col < args.N) {
+            if (rotate) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  const float cs = cr[j], sn = sr[j];
-                  const float a = x1[j], b = x2[j];
-                  x1[j] = a * cs - b * sn;
-                  x2[j] = b * cs + a * sn;
-                }
+              for (int j = 0; j < 32; ++j) {
+                const float a = x1[j], b = x2[j];
+                x1[j] = a * cs[j] - b * sn[j];
+                x2[j] = b * cs[j] + a * sn[j];
               }
-              store_bf16x32(out + (long)m * args.ldo + head_col + c * 32, x1);
-              store_bf16x32(out + (long)m * args.ldo + head_col + 64 + c * 32, x2);
             }
+            store_bf16x32(out + (long)m * args.ldo + head_col + c * 32, x1);
+            store_bf16x32(out + (long)m * args.ldo + head_col + 64 + c * 32, x2);
           }
         }
       } else if constexpr (EPI == EPI_SWIGLU) {
@@ -368,7 +380,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(args.out);
         __nv_bfloat16* hout = reinterpret_cast<__nv_bfloat16*>(args.out2);
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = half * 2; c < half * 2 + 2; ++c) {
           float g[32], u[32];
           tmem_load_f32x32(taddr + c * 32, g);
           tmem_load_f32x32(taddr + 128 + c * 32, u);
@@ -389,14 +401,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
         __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float dh[32];
-          tmem_load_f32x32(taddr + c * 32, dh);
+        for (int c = half * 4; c < half * 4 + 4; ++c) {
           const int f = nt * BN + c * 32;
-          if (row_ok && f < args.N) {
-            float g[32], u[32];
+          const bool ok = row_ok && f < args.N;
+          float g[32], u[32], dh[32];
+          if (ok) {  // issue the global loads before the TMEM load to overlap their latency
             load_bf16x32(args.aux + (long)m * args.ldaux + f, g);
             load_bf16x32(args.aux + (long)m * args.ldaux + args.pair_offset + f, u);
+          }
+          tmem_load_f32x32(taddr + c * 32, dh);
+          if (ok) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float sg = 1.0f / (1.0f + __expf(-g[j]));
@@ -411,13 +425,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       } else if constexpr (EPI == EPI_CE) {
+        // Partial softmax statistics over this warp's 128 columns; partial index nt*2 + half.
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
         const int label = row_ok ? args.labels[m] : -1;
         float run_max = -INFINITY, run_sum = 0.0f;
         int run_arg = 0;
         constexpr float kLog2e = 1.4426950408889634f;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * 4; c < half * 4 + 4; ++c) {
           float v[32];
           tmem_load_f32x32(taddr + c * 32, v);
           const int n = nt * BN + c * 32;
@@ -444,7 +459,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
         if (row_ok) {
-          const long idx = (long)nt * args.M + m;
+          const long idx = (long)(nt * 2 + half) * args.M + m;
           args.ce_max[idx] = run_max;
           args.ce_sum[idx] = run_sum;
           args.ce_arg[idx] = run_arg;

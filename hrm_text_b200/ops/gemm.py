@@ -97,11 +97,11 @@ def linear_wgrad_(dy: Tensor, x: Tensor, grad: Tensor) -> Tensor:
 
 
 def lm_head_ce_logits(x: Tensor, w: Tensor, labels: Tensor):
-    """Logits ``x @ w.T`` (bf16) plus per-256-column partial softmax statistics."""
+    """Logits ``x @ w.T`` (bf16) plus per-128-column partial softmax statistics."""
     _check(x, w)
     M, K = x.shape
     V = w.shape[0]
-    n_tiles = (V + 255) // 256
+    n_tiles = 2 * ((V + 255) // 256)
     logits = torch.empty((M, V), dtype=torch.bfloat16, device=x.device)
     pmax = torch.empty((n_tiles, M), dtype=torch.float32, device=x.device)
     psum = torch.empty((n_tiles, M), dtype=torch.float32, device=x.device)
