@@ -1,0 +1,469 @@
+// PrefixLM packed-varlen flash attention forward on 5th-generation tensor cores (tcgen05).
+//
+// Same contract as attn_fwd in attention.cu (mask: key j visible to query i of a document
+// with prefix P iff j < max(P, i + 1); O, Y = sigmoid(gate) * O and a log2-domain LSE per
+// (head, token); zero rows for padding), same device-built work schedule (LPT-ordered
+// 128-query tiles, layout: 8 header ints then int4 {doc_start, len, prefix, q0} tiles).
+//
+// One CTA = one 128-query tile of one head, persistent over a static stride of the
+// LPT-sorted tile list. Warp roles (192 threads):
+//   warp 0      TMA loads: Q tile once, K and V blocks of 128 keys through 2-stage rings
+//               (128B-swizzled [128 rows][64] boxes straight from the fused gqkv buffer)
+//   warp 1      UMMA issue (one lane): S_j = Q K_j^T into one of two TMEM S buffers, then
+//               O += P_{j-1} V_{j-1}, so S_j runs on the tensor cores while the softmax
+//               warps turn S_{j-1} into P_{j-1}
+//   warps 2..5  softmax, one query row per thread (TMEM lane quarter = warp % 4): reads S
+//               from TMEM twice (row max, then exp2), writes P (bf16) into a K-major
+//               swizzled shared-memory tile for the PV UMMA; keeps the running max m_used
+//               and sum l, and rescales the O row in TMEM only when the row max grows by
+//               more than 8 (log2 units) -- exact, since O and l share the stale max;
+//               finally normalises O, applies the gate and writes O, Y and LSE.
+// TMEM: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+// Shared memory: Q 32 KB, K 2 x 32 KB, V 2 x 32 KB, P 32 KB.
+//
+// Every mbarrier wait is bounded; on a timeout the CTA records an error, drains its own
+// copies and UMMAs, frees TMEM and returns.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace hrm {
+namespace attn_tc {
+
+constexpr int D = 128, BQ = 128, BKV = 128;
+constexpr int SCHED_HEADER = 8;
+constexpr int THREADS = 192;
+constexpr int TILE_BYTES = 128 * 128 * 2;  // one [128][128] bf16 tile = two [128][64] swizzled boxes
+constexpr int SMEM_BYTES = 1024 + 6 * TILE_BYTES + 512;
+constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_O = 256, TM_COLS = 512;
+constexpr float kRescaleThreshold = 8.0f;
+
+// mbarrier wait whose outcome is the same for every lane of the warp (the softmax warps run
+// warp-collective TMEM instructions after their waits and must not diverge on a timeout).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
+      " %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(taddr, r);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+struct Params {
+  __nv_bfloat16* out;
+  __nv_bfloat16* y;
+  const __nv_bfloat16* qkv;  // for the gate
+  long ld_out, ld_qkv;
+  float* lse;
+  int T, H;
+  float scale_log2;
+  const int* sched;
+  int* err;
+};
+
+struct Barriers {
+  uint64_t q_full, q_empty;
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full[2], s_free[2];
+  uint64_t p_full, o_done, o_free, drain;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + TILE_BYTES;          // 2 stages
+  uint8_t* sV = smem + 3 * TILE_BYTES;      // 2 stages
+  uint8_t* sP = smem + 5 * TILE_BYTES;
+  Barriers* bar = reinterpret_cast<Barriers*>(smem + 6 * TILE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = p.sched[0];
+  const int n_items = n_tiles * p.H;
+  const int4* tiles = reinterpret_cast<const int4*>(p.sched + SCHED_HEADER);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    mbar_init(&bar->q_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->k_empty[s], 1);
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->v_empty[s], 1);
+      mbar_init(&bar->s_full[s], 1);
+      mbar_init(&bar->s_free[s], 128);
+    }
+    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->o_done, 1);
+    mbar_init(&bar->o_free, 128);
+    mbar_init(&bar->drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_qkv);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // number of 128-key blocks of a tile
+  auto tile_blocks = [&](const int4& t) {
+    const int kmax = min(t.y, max(t.z, t.w + BQ));
+    return (kmax + BKV - 1) / BKV;
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA loads
+    if (lane == 0) {
+      int n = 0, kv = 0;
+      int last_q = -1, last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        const int4 t = tiles[item / p.H];
+        const int head = item % p.H;
+        const int qx = (p.H + head) * D, kx = (2 * p.H + head) * D, vx = (3 * p.H + head) * D;
+        if (!mbar_wait(&bar->q_empty, (n & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 11); ok = false; break; }
+        mbar_arrive_expect_tx(&bar->q_full, TILE_BYTES);
+        tma_load_2d(sQ, &tm_qkv, &bar->q_full, qx, t.x + t.w);
+        tma_load_2d(sQ + TILE_BYTES / 2, &tm_qkv, &bar->q_full, qx + 64, t.x + t.w);
+        last_q = n;
+        const int nb = tile_blocks(t);
+        for (int j = 0; j < nb; ++j, ++kv) {
+          const int s = kv & 1, r = kv >> 1;
+          const int row = t.x + j * BKV;
+          if (!mbar_wait(&bar->k_empty[s], (r & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 12); ok = false; break; }
+          mbar_arrive_expect_tx(&bar->k_full[s], TILE_BYTES);
+          tma_load_2d(sK + s * TILE_BYTES, &tm_qkv, &bar->k_full[s], kx, row);
+          tma_load_2d(sK + s * TILE_BYTES + TILE_BYTES / 2, &tm_qkv, &bar->k_full[s], kx + 64, row);
+          last_k[s] = r;
+          if (!mbar_wait(&bar->v_empty[s], (r & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 13); ok = false; break; }
+          mbar_arrive_expect_tx(&bar->v_full[s], TILE_BYTES);
+          tma_load_2d(sV + s * TILE_BYTES, &tm_qkv, &bar->v_full[s], vx, row);
+          tma_load_2d(sV + s * TILE_BYTES + TILE_BYTES / 2, &tm_qkv, &bar->v_full[s], vx + 64, row);
+          last_v[s] = r;
+        }
+      }
+      if (!ok) {  // drain this thread's copies in flight
+        if (last_q >= 0) mbar_wait(&bar->q_full, last_q & 1);
+        for (int s = 0; s < 2; ++s) {
+          if (last_k[s] >= 0) mbar_wait(&bar->k_full[s], last_k[s] & 1);
+          if (last_v[s] >= 0) mbar_wait(&bar->v_full[s], last_v[s] & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- UMMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, 0, 0);   // Q K^T: both K-major over d
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(128, 128, 0, 1);  // P V: P K-major over keys, V MN-major
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sP);
+      int n = 0, kv = 0;
+      bool ok = true;
+      auto wait_or_fail = [&](uint64_t* b, uint32_t par, int site) {
+        if (mbar_wait(b, par)) return true;
+        report_error(p.err, kErrAttnWaitTimeout, site);
+        ok = false;
+        return false;
+      };
+      // O += P V for block `blk` (global block counter) of stage s; first block of an item overwrites O
+      auto issue_pv = [&](int blk, bool first) -> bool {
+        const int s = blk & 1, r = blk >> 1;
+        if (!wait_or_fail(&bar->p_full, blk & 1, 21)) return false;
+        if (!wait_or_fail(&bar->v_full[s], r & 1, 22)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // 16 keys per step
+          const uint64_t a = umma_desc_sw128(p_base + (k >> 2) * (TILE_BYTES / 2) + (k & 3) * 32, 16, 1024);
+          const uint64_t b = umma_desc_sw128(v_base + s * TILE_BYTES + k * 2048, TILE_BYTES / 2, 1024);
+          umma_f16_ss(tmem + TM_O, a, b, idesc_pv, (first && k == 0) ? 0u : 1u);
+        }
+        umma_commit(&bar->v_empty[s]);
+        umma_commit(&bar->o_done);
+        return true;
+      };
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        const int4 t = tiles[item / p.H];
+        const int nb = tile_blocks(t);
+        if (!wait_or_fail(&bar->q_full, n & 1, 23)) break;
+        const int first_blk = kv;
+        for (int j = 0; j < nb && ok; ++j, ++kv) {
+          const int s = kv & 1, r = kv >> 1;
+          if (!wait_or_fail(&bar->k_full[s], r & 1, 24)) break;
+          if (!wait_or_fail(&bar->s_free[s], (r & 1) ^ 1, 25)) break;
+          tc_fence_after();
+          const uint32_t d_s = tmem + (s ? TM_S1 : TM_S0);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {  // 16 dims per step
+            const uint32_t off = (k >> 2) * (TILE_BYTES / 2) + (k & 3) * 32;
+            umma_f16_ss(d_s, umma_desc_sw128(q_base + off, 16, 1024),
+                        umma_desc_sw128(k_base + s * TILE_BYTES + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&bar->k_empty[s]);
+          umma_commit(&bar->s_full[s]);
+          if (j == nb - 1) umma_commit(&bar->q_empty);
+          if (j > 0) {
+            if (j == 1 && !wait_or_fail(&bar->o_free, (n & 1) ^ 1, 26)) break;
+            if (!issue_pv(kv - 1, j == 1)) break;
+          }
+        }
+        if (!ok) break;
+        if (nb == 1 && !wait_or_fail(&bar->o_free, (n & 1) ^ 1, 26)) break;
+        if (!issue_pv(kv - 1, nb == 1)) break;
+        (void)first_blk;
+      }
+      umma_commit(&bar->drain);
+      mbar_wait(&bar->drain, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax / epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float sl = p.scale_log2;
+    int n = 0, kv = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      const int4 t = tiles[item / p.H];
+      const int head = item % p.H;
+      const int doc_start = t.x, len = t.y, prefix = t.z, q0 = t.w;
+      const int nb = tile_blocks(t);
+      const int qi = q0 + row;                         // doc-relative query of this thread
+      const int limit = min(len, max(prefix, qi + 1));  // keys [0, limit) are visible
+      const int full_until = min(len, max(prefix, q0 + 1));
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < nb; ++j, ++kv) {
+        const int s = kv & 1;
+        if (!warp_wait(&bar->s_full[s], (kv >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 31); ok = false; break; }
+        tc_fence_after();
+        const uint32_t ts = tmem + lane_off + (s ? TM_S1 : TM_S0);
+        const int k0 = j * BKV;
+        const bool masked = k0 + BKV > full_until;
+        // pass 1: block row max
+        float bmax = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(ts + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const bool vis = !masked || (k0 + c * 32 + e < limit);
+            if (vis) bmax = fmaxf(bmax, v[e] * sl);
+          }
+        }
+        // P_j overwrites P_{j-1}: wait for the previous PV (also guards the O rescale)
+        if (!warp_wait(&bar->o_done, (kv - 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 32); ok = false; break; }
+        tc_fence_after();
+        // The rescale decision is per row, but tcgen05.ld/st are warp-collective
+        // (.sync.aligned): decide per warp, and let rows that need no rescale use alpha = 1.
+        const bool need = bmax > m_used + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? fast_exp2(m_used - bmax) : 1.f;  // 0 on the first block
+          if (j > 0) {
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(tmem + lane_off + TM_O + c * 32, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+              tmem_st_32x32b_x32(tmem + lane_off + TM_O + c * 32, r);
+            }
+            tmem_st_wait();
+          }
+          if (need) {
+            l *= alpha;
+            m_used = bmax;
+          }
+        }
+        // pass 2: P = exp2(s - m_used) -> bf16 K-major swizzled tile (row = query, 128B rows per 64 keys)
+        const float m_safe = m_used == -INFINITY ? 0.f : m_used;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(ts + c * 32, v);
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const bool vis0 = !masked || (k0 + c * 32 + e < limit);
+            const bool vis1 = !masked || (k0 + c * 32 + e + 1 < limit);
+            const float p0 = vis0 ? fast_exp2(v[e] * sl - m_safe) : 0.f;
+            const float p1 = vis1 ? fast_exp2(v[e + 1] * sl - m_safe) : 0.f;
+            l += p0 + p1;
+            pk[e >> 1] = pack_bf16x2(p0, p1);
+          }
+          uint8_t* prow = sP + (c >> 1) * (TILE_BYTES / 2) + row * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int piece = (c & 1) * 4 + q;
+            *reinterpret_cast<uint4*>(prow + ((piece ^ (row & 7)) << 4)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bar->s_free[s]);
+        mbar_arrive(&bar->p_full);
+      }
+      if (!ok) break;
+      // epilogue: wait for the last PV, normalise, gate, write O / Y / LSE
+      if (!warp_wait(&bar->o_done, (kv - 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 33); ok = false; break; }
+      tc_fence_after();
+      const bool row_ok = qi < len;
+      const long tok = (long)doc_start + qi;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tmem + lane_off + TM_O + c * 32, v);
+        if (row_ok) {
+          __nv_bfloat16* orow = p.out + tok * p.ld_out + head * D + c * 32;
+          __nv_bfloat16* yrow = p.y + tok * p.ld_out + head * D + c * 32;
+          const uint4* grow = reinterpret_cast<const uint4*>(p.qkv + tok * p.ld_qkv + head * D + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 gv = grow[q];
+            const uint32_t* ga = &gv.x;
+            uint32_t ow[4], yw[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const float o0 = bf16_round(v[8 * q + 2 * w] * inv), o1 = bf16_round(v[8 * q + 2 * w + 1] * inv);
+              const float2 g = unpack_bf16x2(ga[w]);
+              ow[w] = pack_bf16x2(o0, o1);
+              yw[w] = pack_bf16x2(o0 * sigmoidf_(g.x), o1 * sigmoidf_(g.y));
+            }
+            reinterpret_cast<uint4*>(orow)[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            reinterpret_cast<uint4*>(yrow)[q] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+          }
+        }
+      }
+      if (row_ok) p.lse[(long)head * p.T + tok] = m_used + __log2f(l);
+      tc_fence_before();
+      mbar_arrive(&bar->o_free);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
+// Zero O, Y and LSE of padding tokens [total, T).
+__global__ void zero_tail_kernel(__nv_bfloat16* out, __nv_bfloat16* y, long ld_out, float* lse, int T, int H,
+                                 const int* sched) {
+  const int total = sched[2];
+  const int chunks = H * D / 8;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < (long)(T - total) * chunks;
+       i += (long)gridDim.x * blockDim.x) {
+    const long tok = total + i / chunks;
+    const int c = (int)(i % chunks) * 8;
+    *reinterpret_cast<uint4*>(out + tok * ld_out + c) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(y + tok * ld_out + c) = make_uint4(0, 0, 0, 0);
+  }
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < (long)(T - total) * H;
+       i += (long)gridDim.x * blockDim.x)
+    lse[(long)(i % H) * T + total + i / H] = 0.f;
+}
+
+}  // namespace attn_tc
+
+at::Tensor device_error_word();
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn_attn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    TORCH_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+                    ptr != nullptr,
+                "cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+}  // namespace
+
+void attn_fwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
+                 const at::Tensor& y, const at::Tensor& lse) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(1) == 1, "qkv must be row-major bf16");
+  TORCH_CHECK((qkv.stride(0) * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(qkv.data_ptr()) & 15) == 0,
+              "qkv rows must be 16-byte aligned");
+  TORCH_CHECK(qkv.size(1) >= 4 * H * attn_tc::D, "qkv width");
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int T = (int)qkv.size(0);
+
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)qkv.size(1), (cuuint64_t)T};
+  cuuint64_t strides[1] = {(cuuint64_t)(qkv.stride(0) * 2)};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn_attn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+
+  attn_tc::Params p{};
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  TORCH_CHECK(out.stride(0) == y.stride(0), "O and Y must share a row stride");
+  p.ld_out = out.stride(0);
+  p.ld_qkv = qkv.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.T = T;
+  p.H = (int)H;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)attn_tc::D));
+  p.sched = sched.data_ptr<int>();
+  p.err = device_error_word().data_ptr<int>();
+
+  static bool configured = false;
+  if (!configured) {
+    TORCH_CHECK(cudaFuncSetAttribute(attn_tc::attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn_tc::SMEM_BYTES) == cudaSuccess,
+                "cudaFuncSetAttribute failed");
+    configured = true;
+  }
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  attn_tc::attn_fwd_tc_kernel<<<sms, attn_tc::THREADS, attn_tc::SMEM_BYTES, stream>>>(map, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  attn_tc::zero_tail_kernel<<<64, 256, 0, stream>>>(p.out, p.y, p.ld_out, p.lse, T, (int)H, p.sched);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace hrm

@@ -14,6 +14,8 @@ int64_t attn_schedule_capacity(int64_t T, int64_t n_cu);
 void attn_schedule(const at::Tensor& cu_seqlens, const at::Tensor& prefix_lens, bool causal, const at::Tensor& sched);
 void attn_fwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out, const at::Tensor& y,
               const at::Tensor& lse);
+void attn_fwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
+                 const at::Tensor& y, const at::Tensor& lse);
 void attn_bwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
               const at::Tensor& lse, const at::Tensor& dy, const at::Tensor& positions, const at::Tensor& cos_tab,
               const at::Tensor& sin_tab, const at::Tensor& d_out, const at::Tensor& dsum, const at::Tensor& dq_acc,
@@ -41,6 +43,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_schedule_capacity", &hrm::attn_schedule_capacity);
   m.def("attn_schedule", &hrm::attn_schedule);
   m.def("attn_fwd", &hrm::attn_fwd);
+  m.def("attn_fwd_tc", &hrm::attn_fwd_tc, "tcgen05 PrefixLM attention forward");
   m.def("attn_bwd", &hrm::attn_bwd);
   m.def("rmsnorm_fwd", &hrm::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &hrm::rmsnorm_bwd);

@@ -298,7 +298,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for_each_segment(sched, stream_k, [&](int tile, int kb0, int kb1) -> bool {
       const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
       const int acc = local & 1, use = local >> 1;
-      if (!mbar_wait(&tfull_bar[acc], use & 1)) {
+      // warp-uniform outcome: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[acc], use & 1))) {
         report_error(args.err, kErrGemmWaitTimeout, 4);
         return false;
       }

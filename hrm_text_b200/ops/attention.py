@@ -59,14 +59,22 @@ def rope_half_tables(module: torch.nn.Module) -> tuple[Tensor, Tensor]:
     return tabs
 
 
-def attention_fwd(gqkv: Tensor, num_heads: int, sched: Tensor):
-    """Returns ``(O, Y = sigmoid(gate) * O, lse)`` for the packed ``gqkv [T, 4*H*128]``."""
+def attention_fwd(gqkv: Tensor, num_heads: int, sched: Tensor, kernel: str = "tcgen05"):
+    """Returns ``(O, Y = sigmoid(gate) * O, lse)`` for the packed ``gqkv [T, 4*H*128]``.
+
+    ``kernel="tcgen05"`` (training path) runs the TMEM/UMMA kernel (attention_tc.cu);
+    ``kernel="mma"`` runs the warp-level mma.sync kernel (attention.cu), kept as a
+    cross-check and as the kernel behind the allocation-free C entry point.
+    """
     T = gqkv.shape[0]
     width = num_heads * 128
     out = torch.empty((T, width), dtype=torch.bfloat16, device=gqkv.device)
     y = torch.empty_like(out)
     lse = torch.empty((num_heads, T), dtype=torch.float32, device=gqkv.device)
-    cuda().attn_fwd(gqkv, num_heads, sched, out, y, lse)
+    if kernel == "tcgen05":
+        cuda().attn_fwd_tc(gqkv, num_heads, sched, out, y, lse)
+    else:
+        cuda().attn_fwd(gqkv, num_heads, sched, out, y, lse)
     return out, y, lse
 
 

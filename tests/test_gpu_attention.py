@@ -26,3 +26,45 @@ def test_attention_fwd_bwd(cuda_device, causal):
     for a, b, name in ((q.grad, qr.grad, "dq"), (k.grad, kr.grad, "dk"), (v.grad, vr.grad, "dv")):
         assert_close(a, b, 3e-2, name)
         assert a[total:].abs().max().item() == 0.0
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_tcgen05_forward_matches_mma_forward(cuda_device, causal):
+    """The tcgen05 forward against the mma.sync forward on a long packed batch (docs up to 4096)."""
+    from hrm_text_b200.ops.attention import PackedSeq, attention_fwd
+    torch.manual_seed(1)
+    T, H = 8192, 3
+    cu, pl, pos, total = random_packing(T, seed=7, max_doc=4096)
+    packed = PackedSeq(pos.to(cuda_device), cu.to(cuda_device), pl.to(cuda_device))
+    qkv = torch.randn(T, 4 * H * 128, device=cuda_device).bfloat16()
+    a = attention_fwd(qkv, H, packed.schedule(causal), kernel="tcgen05")
+    b = attention_fwd(qkv, H, packed.schedule(causal), kernel="mma")
+    for x, y, name in zip(a, b, ("O", "Y", "lse")):
+        assert_close(x[:total] if name != "lse" else x[:, :total], y[:total] if name != "lse" else y[:, :total],
+                     2e-2, name)
+    assert a[0][total:].abs().max().item() == 0.0
+
+
+def test_tcgen05_forward_bench_shape_with_rescales(cuda_device):
+    """Bench-sized launch (T=21504, 10 heads, many tiles per CTA) with key magnitudes growing
+    along each document, so row maxima rise block after block and rows rescale at different
+    blocks (exercises the warp-uniform lazy-rescale path)."""
+    from hrm_text_b200.data.synthetic import packed_batches
+    from hrm_text_b200.ops.attention import PackedSeq, attention_fwd
+    torch.manual_seed(2)
+    T, H = 21504, 10
+    b, s = next(iter(packed_batches(T, 32768, 4096, num_batches=1, seed=5)))
+    total = s["total_seqlen"]
+    packed = PackedSeq(b["position_ids"].to(cuda_device), b["cu_seqlens"].to(cuda_device),
+                       b["prefix_lens"].to(cuda_device))
+    qkv = torch.randn(T, 4, H, 128, device=cuda_device)
+    growth = 1.0 + b["position_ids"].to(cuda_device).float()[:, None, None] / 300.0
+    qkv[:, 2] *= growth  # keys
+    qkv = qkv.reshape(T, 4 * H * 128).bfloat16()
+    a = attention_fwd(qkv, H, packed.schedule(False), kernel="tcgen05")
+    ref = attention_fwd(qkv, H, packed.schedule(False), kernel="mma")
+    torch.cuda.synchronize()
+    from hrm_text_b200.utils.errors import check_device_errors
+    check_device_errors()
+    assert_close(a[0][:total], ref[0][:total], 2e-2, "O")
+    assert_close(a[2][:, :total], ref[2][:, :total], 1e-3, "lse")

@@ -39,7 +39,7 @@ def test_noalloc_matches_regular_forward(cuda_device, causal):
     cu, pl, pos, total = random_packing(T, seed=3)
     cu, pl, pos = cu.to(cuda_device), pl.to(cuda_device), pos.to(cuda_device)
     qkv = torch.randn(T, 4 * H * 128, device=cuda_device).bfloat16()
-    ref_out, ref_y, ref_lse = attention_fwd(qkv, H, PackedSeq(pos, cu, pl).schedule(causal))
+    ref_out, ref_y, ref_lse = attention_fwd(qkv, H, PackedSeq(pos, cu, pl).schedule(causal), kernel="mma")
     stream = torch.cuda.current_stream(cuda_device)
     for _ in range(2):  # two calls in a row share (and must re-initialise) the static scratch
         out = torch.full_like(ref_out, 7.0)
