@@ -1,0 +1,82 @@
+"""PrefixLM attention microbenchmark.
+
+    python -m hrm_text_b200.benchmarks.attention [--heads 16] [--tokens 21504] [--iters 20]
+        [--kernel tcgen05|mma] [--only fwd|bwd|both]
+
+bf16, head_dim 128, ``tokens`` packed tokens (documents log-normal, median 512, clipped to
+[16, 4096], prefix fraction U[0, 0.5]), Q/K/V ~ N(0, 1) from seed 0. Each phase is timed
+with CUDA events over ``iters`` launches after warm-up; reported with its useful FLOPs
+(visible query-key pairs: 4 * pairs * 128 per head forward, 2.5x that backward).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def visible_pairs(cu, pl, n_docs) -> int:
+    total = 0
+    for i in range(n_docs):
+        L = int(cu[i + 1] - cu[i])
+        P = int(pl[i])
+        total += P * P  # prefix queries see the whole prefix
+        total += (L * (L + 1) - P * (P + 1)) // 2  # response query q sees keys [0, q]
+    return total
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--tokens", type=int, default=21504)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--kernel", default="tcgen05", choices=["tcgen05", "mma"])
+    ap.add_argument("--only", default="both", choices=["fwd", "bwd", "both"])
+    args = ap.parse_args(argv)
+
+    from ..data.synthetic import packed_batches
+    from ..ops.attention import PackedSeq, attention_bwd, attention_fwd
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    T, H = args.tokens, args.heads
+    b, s = next(iter(packed_batches(T, 32768, 4096, num_batches=1, seed=0)))
+    packed = PackedSeq(b["position_ids"].to(dev), b["cu_seqlens"].to(dev), b["prefix_lens"].to(dev))
+    sched = packed.schedule(False)
+    qkv = torch.randn(T, 4 * H * 128, device=dev).bfloat16()
+    pairs = visible_pairs(b["cu_seqlens"].tolist(), b["prefix_lens"].tolist(), s["numseqs"])
+    fwd_flop = 4.0 * pairs * 128 * H
+    cos = torch.ones(4096, 64, device=dev)
+    sin = torch.zeros(4096, 64, device=dev)
+    out = {"tokens": T, "heads": H, "docs": s["numseqs"], "visible_pairs": pairs, "kernel": args.kernel}
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.iters
+
+    o, y, lse = attention_fwd(qkv, H, sched, kernel=args.kernel)
+    if args.only in ("fwd", "both"):
+        ms = timed(lambda: attention_fwd(qkv, H, sched, kernel=args.kernel))
+        out["fwd_ms"] = ms
+        out["fwd_tflops"] = fwd_flop / ms / 1e9
+    if args.only in ("bwd", "both"):
+        dy = torch.randn(T, H * 128, device=dev).bfloat16()
+        ms = timed(lambda: attention_bwd(qkv, H, sched, o, lse, dy, packed.position_ids, cos, sin))
+        out["bwd_ms"] = ms
+        out["bwd_tflops"] = 2.5 * fwd_flop / ms / 1e9
+    from ..utils.errors import check_device_errors
+    check_device_errors()
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()
