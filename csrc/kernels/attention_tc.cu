@@ -394,6 +394,357 @@ __global__ void zero_tail_kernel(__nv_bfloat16* out, __nv_bfloat16* y, long ld_o
     lse[(long)(i % H) * T + total + i / H] = 0.f;
 }
 
+
+// =======================================================================================
+// Backward (tcgen05). One CTA = one 128-key block of one head (LPT-sorted key-block list),
+// looping over the 64-query blocks that can see those keys. Per query block b:
+//   S^T  = K Q^T      (M=128 keys, N=64 queries, K=128 dims)  -> TMEM
+//   dP^T = V dO^T     (same shape)                              -> TMEM
+//   softmax warps (row = key): P^T = exp2(S^T * scale_log2 - lse[q]) (masked to 0),
+//     dS^T = P^T * (dP^T - D[q]) * scale  -> bf16, K-major swizzled smem tiles
+//   dV  += P^T dO     (M=128 keys, N=128 dims, K=64 queries)   -> TMEM, whole key block
+//   dK  += dS^T Q     (same shape)                              -> TMEM, whole key block
+//   dQ^T = K^T dS^T   (M=128 dims, N=64 queries, K=128 keys)   -> TMEM; the dQ warps add it
+//     into the fp32 dQ accumulator (coalesced: a warp covers 32 consecutive dims of a query)
+// At the end of the key block the softmax warps apply the RoPE backward to dK and write the
+// dK / dV rows. Warp roles (320 threads): 0 TMA, 1 UMMA, 2-5 softmax + dK/dV epilogue, 6-9 dQ.
+// TMEM: S^T [0,64), dP^T [64,128), dQ^T [128,192), dV [256,384), dK [384,512).
+// Shared: K 32 KB, V 32 KB, Q 2x16 KB, dO 2x16 KB, P^T 16 KB, dS^T 16 KB, lse/D 2x512 B.
+// =======================================================================================
+constexpr int BWD_THREADS = 320;
+constexpr int BQB = 64;                 // queries per block
+constexpr int QTILE_BYTES = BQB * 128 * 2;   // [64][128] bf16 = two [64][64] boxes (16 KB)
+constexpr int PTILE_BYTES = 128 * BQB * 2;   // [128 keys][64 queries] bf16 (16 KB)
+constexpr int BWD_SMEM_BYTES = 1024 + 2 * TILE_BYTES + 4 * QTILE_BYTES + 2 * PTILE_BYTES + 2048 + 512;
+constexpr uint32_t TB_S = 0, TB_DP = 64, TB_DQ = 128, TB_DV = 256, TB_DK = 384;
+
+struct BwdParams {
+  __nv_bfloat16* dqkv;
+  long ld_dqkv;
+  const float* lse;   // [H, T] log2 domain
+  const float* dsum;  // [H, T]
+  float* dq_acc;      // [T, H*128]
+  const int* positions;
+  const float* cos_tab;  // [S, 64]
+  const float* sin_tab;
+  int T, H;
+  float scale, scale_log2;
+  const int* sched;
+  int cap;
+  int* err;
+};
+
+struct BwdBarriers {
+  uint64_t kv_full, kv_done, kv_free;
+  uint64_t qd_full[2], qd_empty[2];
+  uint64_t s_full, s_free, p_full, p_free, dq_full, dq_free, drain;
+};
+
+__device__ __forceinline__ int bwd_qstart(const int4& t) { return t.w < t.z ? 0 : t.w; }
+__device__ __forceinline__ int bwd_nqb(const int4& t) { return (t.y - bwd_qstart(t) + BQB - 1) / BQB; }
+
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE_BYTES;
+  uint8_t* sQ = sV + TILE_BYTES;               // 2 stages
+  uint8_t* sDO = sQ + 2 * QTILE_BYTES;         // 2 stages
+  uint8_t* sP = sDO + 2 * QTILE_BYTES;
+  uint8_t* sDS = sP + PTILE_BYTES;
+  float* sLse = reinterpret_cast<float*>(sDS + PTILE_BYTES);  // per softmax warp: [64] lse, [64] D
+  BwdBarriers* bar = reinterpret_cast<BwdBarriers*>(sLse + 512);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_items = p.sched[1] * p.H;
+  const int4* tiles = reinterpret_cast<const int4*>(p.sched + SCHED_HEADER) + p.cap;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->kv_full, 1);
+    mbar_init(&bar->kv_done, 1);
+    mbar_init(&bar->kv_free, 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->qd_full[s], 1);
+      mbar_init(&bar->qd_empty[s], 1);
+    }
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->s_free, 128);
+    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->p_free, 1);
+    mbar_init(&bar->dq_full, 1);
+    mbar_init(&bar->dq_free, 128);
+    mbar_init(&bar->drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_kv);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_do);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA loads
+    if (lane == 0) {
+      int n = 0, qb_all = 0;
+      int last_kv = -1, last_q[2] = {-1, -1};
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        const int4 t = tiles[item / p.H];
+        const int head = item % p.H;
+        const int qx = (p.H + head) * D, kx = (2 * p.H + head) * D, vx = (3 * p.H + head) * D;
+        if (!mbar_wait(&bar->kv_done, (n & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 41); ok = false; break; }
+        mbar_arrive_expect_tx(&bar->kv_full, 2 * TILE_BYTES);
+        const int krow = t.x + t.w;
+        tma_load_2d(sK, &tm_kv, &bar->kv_full, kx, krow);
+        tma_load_2d(sK + TILE_BYTES / 2, &tm_kv, &bar->kv_full, kx + 64, krow);
+        tma_load_2d(sV, &tm_kv, &bar->kv_full, vx, krow);
+        tma_load_2d(sV + TILE_BYTES / 2, &tm_kv, &bar->kv_full, vx + 64, krow);
+        last_kv = n;
+        const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
+        for (int qb = 0; qb < nqb; ++qb, ++qb_all) {
+          const int s = qb_all & 1, r = qb_all >> 1;
+          if (!mbar_wait(&bar->qd_empty[s], (r & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 42); ok = false; break; }
+          mbar_arrive_expect_tx(&bar->qd_full[s], 2 * QTILE_BYTES);
+          const int qrow = t.x + qs + qb * BQB;
+          tma_load_2d(sQ + s * QTILE_BYTES, &tm_q, &bar->qd_full[s], qx, qrow);
+          tma_load_2d(sQ + s * QTILE_BYTES + QTILE_BYTES / 2, &tm_q, &bar->qd_full[s], qx + 64, qrow);
+          tma_load_2d(sDO + s * QTILE_BYTES, &tm_do, &bar->qd_full[s], head * D, qrow);
+          tma_load_2d(sDO + s * QTILE_BYTES + QTILE_BYTES / 2, &tm_do, &bar->qd_full[s], head * D + 64, qrow);
+          last_q[s] = r;
+        }
+      }
+      if (!ok) {
+        if (last_kv >= 0) mbar_wait(&bar->kv_full, last_kv & 1);
+        for (int s = 0; s < 2; ++s)
+          if (last_q[s] >= 0) mbar_wait(&bar->qd_full[s], last_q[s] & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- UMMA issue
+    if (lane == 0) {
+      constexpr uint32_t id_s = umma_idesc_bf16(128, 64, 0, 0);    // S^T, dP^T
+      constexpr uint32_t id_kv = umma_idesc_bf16(128, 128, 0, 1);  // dV, dK
+      constexpr uint32_t id_dq = umma_idesc_bf16(128, 64, 1, 1);   // dQ^T
+      const uint32_t kb = smem_u32(sK), vb = smem_u32(sV), qb0 = smem_u32(sQ), db0 = smem_u32(sDO);
+      const uint32_t pb = smem_u32(sP), dsb = smem_u32(sDS);
+      int n = 0, b = 0;
+      bool ok = true;
+      auto wait_ok = [&](uint64_t* x, uint32_t par, int site) {
+        if (mbar_wait(x, par)) return true;
+        report_error(p.err, kErrAttnWaitTimeout, site);
+        ok = false;
+        return false;
+      };
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        const int4 t = tiles[item / p.H];
+        const int nqb = bwd_nqb(t);
+        if (!wait_ok(&bar->kv_full, n & 1, 51)) break;
+        for (int qb = 0; qb < nqb; ++qb, ++b) {
+          const int s = b & 1, r = b >> 1;
+          if (!wait_ok(&bar->qd_full[s], r & 1, 52)) break;
+          if (!wait_ok(&bar->s_free, (b & 1) ^ 1, 53)) break;
+          tc_fence_after();
+          const uint32_t qs = qb0 + s * QTILE_BYTES, ds = db0 + s * QTILE_BYTES;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {  // 16 dims per step
+            const uint32_t oa = (k >> 2) * (TILE_BYTES / 2) + (k & 3) * 32;
+            const uint32_t ob = (k >> 2) * (QTILE_BYTES / 2) + (k & 3) * 32;
+            umma_f16_ss(tmem + TB_S, umma_desc_sw128(kb + oa, 16, 1024), umma_desc_sw128(qs + ob, 16, 1024), id_s,
+                        k > 0);
+            umma_f16_ss(tmem + TB_DP, umma_desc_sw128(vb + oa, 16, 1024), umma_desc_sw128(ds + ob, 16, 1024), id_s,
+                        k > 0);
+          }
+          umma_commit(&bar->s_full);
+          if (!wait_ok(&bar->p_full, b & 1, 54)) break;
+          if (qb == 0 && !wait_ok(&bar->kv_free, (n & 1) ^ 1, 55)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {  // 16 queries per step
+            const uint64_t bo = umma_desc_sw128(ds + k * 2048, QTILE_BYTES / 2, 1024);
+            const uint64_t bq = umma_desc_sw128(qs + k * 2048, QTILE_BYTES / 2, 1024);
+            const uint32_t acc = (qb > 0 || k > 0) ? 1u : 0u;
+            umma_f16_ss(tmem + TB_DV, umma_desc_sw128(pb + k * 32, 16, 1024), bo, id_kv, acc);
+            umma_f16_ss(tmem + TB_DK, umma_desc_sw128(dsb + k * 32, 16, 1024), bq, id_kv, acc);
+          }
+          if (!wait_ok(&bar->dq_free, (b & 1) ^ 1, 56)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {  // 16 keys per step
+            umma_f16_ss(tmem + TB_DQ, umma_desc_sw128(kb + k * 2048, TILE_BYTES / 2, 1024),
+                        umma_desc_sw128(dsb + k * 2048, PTILE_BYTES, 1024), id_dq, k > 0);
+          }
+          umma_commit(&bar->qd_empty[s]);
+          umma_commit(&bar->p_free);
+          umma_commit(&bar->dq_full);
+        }
+        if (!ok) break;
+        umma_commit(&bar->kv_done);
+      }
+      umma_commit(&bar->drain);
+      mbar_wait(&bar->drain, 0);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- softmax + dK/dV epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // key within the block
+    const uint32_t lo = (uint32_t)(quarter * 32) << 16;
+    int n = 0, b = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      const int4 t = tiles[item / p.H];
+      const int head = item % p.H;
+      const int doc_start = t.x, len = t.y, prefix = t.z, k0 = t.w;
+      const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
+      const int key = k0 + row;
+      const bool key_ok = key < len;
+      for (int qb = 0; qb < nqb; ++qb, ++b) {
+        const int qbase = qs + qb * BQB;  // doc-relative first query
+        // warp-private copy of this block's lse / D (no cross-warp barrier on this path)
+        float* lse_b = sLse + (warp - 2) * 2 * BQB;
+        float* d_b = lse_b + BQB;
+        __syncwarp();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int j = lane + 32 * h;
+          const int q = qbase + j;
+          const bool qv = q < len;
+          const long idx = (long)head * p.T + doc_start + q;
+          lse_b[j] = qv ? p.lse[idx] : 0.f;
+          d_b[j] = qv ? p.dsum[idx] : 0.f;
+        }
+        __syncwarp();
+        if (!warp_wait(&bar->s_full, b & 1)) { report_error(p.err, kErrAttnWaitTimeout, 61); ok = false; break; }
+        tc_fence_after();
+        uint32_t pp[32], dd[32];  // 64 bf16 each
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float sv[32], dv[32];
+          tmem_ld32(tmem + lo + TB_S + c * 32, sv);
+          tmem_ld32(tmem + lo + TB_DP + c * 32, dv);
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float pr[2], ds[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int j = c * 32 + e + u;
+              const int q = qbase + j;
+              const bool vis = key_ok && q < len && key < max(prefix, q + 1);
+              pr[u] = vis ? fast_exp2(sv[e + u] * p.scale_log2 - lse_b[j]) : 0.f;
+              ds[u] = pr[u] * (dv[e + u] - d_b[j]) * p.scale;
+            }
+            pp[c * 16 + (e >> 1)] = pack_bf16x2(pr[0], pr[1]);
+            dd[c * 16 + (e >> 1)] = pack_bf16x2(ds[0], ds[1]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bar->s_free);
+        if (!warp_wait(&bar->p_free, (b & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 62); ok = false; break; }
+        uint8_t* prow = sP + row * 128;
+        uint8_t* drow = sDS + row * 128;
+#pragma unroll
+        for (int piece = 0; piece < 8; ++piece) {
+          const int off = (piece ^ (row & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + off) =
+              make_uint4(pp[4 * piece], pp[4 * piece + 1], pp[4 * piece + 2], pp[4 * piece + 3]);
+          *reinterpret_cast<uint4*>(drow + off) =
+              make_uint4(dd[4 * piece], dd[4 * piece + 1], dd[4 * piece + 2], dd[4 * piece + 3]);
+        }
+        fence_async_smem();
+        mbar_arrive(&bar->p_full);
+      }
+      if (!ok) break;
+      // dK / dV of this key block: wait for its last MMAs, RoPE-backward dK, write both.
+      if (!warp_wait(&bar->kv_done, n & 1)) { report_error(p.err, kErrAttnWaitTimeout, 63); ok = false; break; }
+      tc_fence_after();
+      const long tok = (long)doc_start + key;
+      const int pos = key_ok ? p.positions[tok] : 0;
+      __nv_bfloat16* dk_row = p.dqkv + tok * p.ld_dqkv + (2 * p.H + head) * D;
+      __nv_bfloat16* dv_row = p.dqkv + tok * p.ld_dqkv + (3 * p.H + head) * D;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {  // dims [c*32, c*32+32) pair with +64
+        float x1[32], x2[32], v1[32], v2[32];
+        tmem_ld32(tmem + lo + TB_DK + c * 32, x1);
+        tmem_ld32(tmem + lo + TB_DK + 64 + c * 32, x2);
+        tmem_ld32(tmem + lo + TB_DV + c * 32, v1);
+        tmem_ld32(tmem + lo + TB_DV + 64 + c * 32, v2);
+        if (key_ok) {
+          const float* cr = p.cos_tab + (long)pos * 64 + c * 32;
+          const float* sr = p.sin_tab + (long)pos * 64 + c * 32;
+          uint32_t a[16], bb[16], va[16], vb2[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float c0 = cr[e], c1 = cr[e + 1], s0 = sr[e], s1 = sr[e + 1];
+            a[e >> 1] = pack_bf16x2(x1[e] * c0 + x2[e] * s0, x1[e + 1] * c1 + x2[e + 1] * s1);
+            bb[e >> 1] = pack_bf16x2(x2[e] * c0 - x1[e] * s0, x2[e + 1] * c1 - x1[e + 1] * s1);
+            va[e >> 1] = pack_bf16x2(v1[e], v1[e + 1]);
+            vb2[e >> 1] = pack_bf16x2(v2[e], v2[e + 1]);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            reinterpret_cast<uint4*>(dk_row + c * 32)[q] = make_uint4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]);
+            reinterpret_cast<uint4*>(dk_row + 64 + c * 32)[q] =
+                make_uint4(bb[4 * q], bb[4 * q + 1], bb[4 * q + 2], bb[4 * q + 3]);
+            reinterpret_cast<uint4*>(dv_row + c * 32)[q] =
+                make_uint4(va[4 * q], va[4 * q + 1], va[4 * q + 2], va[4 * q + 3]);
+            reinterpret_cast<uint4*>(dv_row + 64 + c * 32)[q] =
+                make_uint4(vb2[4 * q], vb2[4 * q + 1], vb2[4 * q + 2], vb2[4 * q + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar->kv_free);
+    }
+  } else {
+    // ---------------------------------------------------------------- dQ accumulation
+    const int quarter = warp & 3;
+    const int dim = quarter * 32 + lane;  // TMEM lane = head dim
+    const uint32_t lo = (uint32_t)(quarter * 32) << 16;
+    int b = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const int4 t = tiles[item / p.H];
+      const int head = item % p.H;
+      const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
+      for (int qb = 0; qb < nqb; ++qb, ++b) {
+        if (!warp_wait(&bar->dq_full, b & 1)) { report_error(p.err, kErrAttnWaitTimeout, 71); ok = false; break; }
+        tc_fence_after();
+        const int qbase = qs + qb * BQB;
+        float* col = p.dq_acc + ((long)t.x + qbase) * (p.H * D) + head * D + dim;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tmem_ld32(tmem + lo + TB_DQ + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int q = qbase + c * 32 + e;
+            if (q < t.y) atomicAdd(col + (long)(c * 32 + e) * (p.H * D), v[e]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bar->dq_free);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
 }  // namespace attn_tc
 
 at::Tensor device_error_word();
@@ -463,6 +814,82 @@ void attn_fwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
   attn_tc::attn_fwd_tc_kernel<<<sms, attn_tc::THREADS, attn_tc::SMEM_BYTES, stream>>>(map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   attn_tc::zero_tail_kernel<<<64, 256, 0, stream>>>(p.out, p.y, p.ld_out, p.lse, T, (int)H, p.sched);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+
+namespace attn {
+__global__ void attn_bwd_pre_kernel(const __nv_bfloat16* dy, const __nv_bfloat16* out, long ld_out,
+                                    const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* d_out,
+                                    __nv_bfloat16* dqkv, long ld_dqkv, float* dsum, float* dq_acc, int T, int H);
+__global__ void attn_bwd_post_kernel(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, const int* positions,
+                                     const float* cos_tab, const float* sin_tab, int T, int H, const int* sched);
+}  // namespace attn
+
+static CUtensorMap make_map_rows(const at::Tensor& t, uint32_t box_rows) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)t.size(1), (cuuint64_t)t.size(0)};
+  cuuint64_t strides[1] = {(cuuint64_t)(t.stride(0) * 2)};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.stride(1) == 1 && (t.stride(0) * 2) % 16 == 0 &&
+                  (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0,
+              "attention operands must be 16-byte aligned row-major bf16");
+  CUresult r = encode_fn_attn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return map;
+}
+
+void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
+                 const at::Tensor& lse, const at::Tensor& dy, const at::Tensor& positions, const at::Tensor& cos_tab,
+                 const at::Tensor& sin_tab, const at::Tensor& d_out, const at::Tensor& dsum, const at::Tensor& dq_acc,
+                 const at::Tensor& dqkv) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int T = (int)qkv.size(0);
+  auto bf = [](const at::Tensor& x) { return reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()); };
+  auto bfm = [](const at::Tensor& x) { return reinterpret_cast<__nv_bfloat16*>(x.data_ptr()); };
+  {
+    const long warps = (long)T * H;
+    const long blocks = (warps * 32 + 255) / 256;
+    attn::attn_bwd_pre_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
+        bf(dy), bf(out), out.stride(0), bf(qkv), qkv.stride(0), bfm(d_out), bfm(dqkv), dqkv.stride(0),
+        dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), T, (int)H);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  const CUtensorMap m_kv = make_map_rows(qkv, 128), m_q = make_map_rows(qkv, 64), m_do = make_map_rows(d_out, 64);
+  attn_tc::BwdParams p{};
+  p.dqkv = bfm(dqkv);
+  p.ld_dqkv = dqkv.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.dsum = dsum.data_ptr<float>();
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.positions = positions.data_ptr<int>();
+  p.cos_tab = cos_tab.data_ptr<float>();
+  p.sin_tab = sin_tab.data_ptr<float>();
+  p.T = T;
+  p.H = (int)H;
+  p.scale = (float)(1.0 / std::sqrt(128.0));
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  p.sched = sched.data_ptr<int>();
+  p.cap = (int)((sched.numel() - attn_tc::SCHED_HEADER) / 8);
+  p.err = device_error_word().data_ptr<int>();
+  static bool configured = false;
+  if (!configured) {
+    TORCH_CHECK(cudaFuncSetAttribute(attn_tc::attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn_tc::BWD_SMEM_BYTES) == cudaSuccess,
+                "cudaFuncSetAttribute failed");
+    configured = true;
+  }
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  attn_tc::attn_bwd_tc_kernel<<<sms, attn_tc::BWD_THREADS, attn_tc::BWD_SMEM_BYTES, stream>>>(m_kv, m_q, m_do, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  attn::attn_bwd_post_kernel<<<1024, 256, 0, stream>>>(p.dq_acc, p.dqkv, p.ld_dqkv, p.positions, p.cos_tab, p.sin_tab, T,
+                                                       (int)H, p.sched);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -79,15 +79,20 @@ def attention_fwd(gqkv: Tensor, num_heads: int, sched: Tensor, kernel: str = "tc
 
 
 def attention_bwd(gqkv: Tensor, num_heads: int, sched: Tensor, out: Tensor, lse: Tensor, dy: Tensor,
-                  positions: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
-    """Gradient w.r.t. the packed ``gqkv`` (gate, q, k, v; RoPE backward applied to q, k)."""
+                  positions: Tensor, cos: Tensor, sin: Tensor, kernel: str = "tcgen05") -> Tensor:
+    """Gradient w.r.t. the packed ``gqkv`` (gate, q, k, v; RoPE backward applied to q, k).
+
+    ``kernel="tcgen05"`` runs the TMEM/UMMA backward (attention_tc.cu); ``"mma"`` the
+    mma.sync backward (attention.cu), kept as a cross-check.
+    """
     T = gqkv.shape[0]
     width = num_heads * 128
     d_out = torch.empty((T, width), dtype=torch.bfloat16, device=gqkv.device)
     dsum = torch.empty((num_heads, T), dtype=torch.float32, device=gqkv.device)
     dq_acc = torch.empty((T, width), dtype=torch.float32, device=gqkv.device)
     dgqkv = torch.empty((T, 4 * width), dtype=torch.bfloat16, device=gqkv.device)
-    cuda().attn_bwd(gqkv, num_heads, sched, out, lse, dy, positions, cos, sin, d_out, dsum, dq_acc, dgqkv)
+    fn = cuda().attn_bwd_tc if kernel == "tcgen05" else cuda().attn_bwd
+    fn(gqkv, num_heads, sched, out, lse, dy, positions, cos, sin, d_out, dsum, dq_acc, dgqkv)
     return dgqkv
 
 

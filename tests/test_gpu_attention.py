@@ -68,3 +68,32 @@ def test_tcgen05_forward_bench_shape_with_rescales(cuda_device):
     check_device_errors()
     assert_close(a[0][:total], ref[0][:total], 2e-2, "O")
     assert_close(a[2][:, :total], ref[2][:, :total], 1e-3, "lse")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_tcgen05_backward_matches_mma_backward(cuda_device, causal):
+    """tcgen05 backward vs mma.sync backward at the bench shape, with real RoPE tables."""
+    from hrm_text_b200.data.synthetic import packed_batches
+    from hrm_text_b200.models.layers import rope_tables
+    from hrm_text_b200.ops.attention import PackedSeq, attention_bwd, attention_fwd
+    from hrm_text_b200.utils.errors import check_device_errors
+    torch.manual_seed(3)
+    T, H = 21504, 10
+    b, s = next(iter(packed_batches(T, 32768, 4096, num_batches=1, seed=9)))
+    total = s["total_seqlen"]
+    packed = PackedSeq(b["position_ids"].to(cuda_device), b["cu_seqlens"].to(cuda_device),
+                       b["prefix_lens"].to(cuda_device))
+    sched = packed.schedule(causal)
+    qkv = torch.randn(T, 4 * H * 128, device=cuda_device).bfloat16()
+    o, y, lse = attention_fwd(qkv, H, sched, kernel="mma")
+    dy = torch.randn(T, H * 128, device=cuda_device).bfloat16()
+    cos, sin = rope_tables(128, 4096, 10000.0, device=cuda_device)
+    cos, sin = cos[:, :64].contiguous(), sin[:, :64].contiguous()
+    g_tc = attention_bwd(qkv, H, sched, o, lse, dy, packed.position_ids, cos, sin, kernel="tcgen05")
+    g_mma = attention_bwd(qkv, H, sched, o, lse, dy, packed.position_ids, cos, sin, kernel="mma")
+    torch.cuda.synchronize()
+    check_device_errors()
+    for part, name in enumerate(("dgate", "dq", "dk", "dv")):
+        sl = slice(part * H * 128, (part + 1) * H * 128)
+        assert_close(g_tc[:total, sl], g_mma[:total, sl], 3e-2, name)
+    assert g_tc[total:].abs().max().item() == 0.0
