@@ -49,6 +49,12 @@ def rmsnorm_bwd(dy: Tensor, s: Tensor, rstd: Tensor, dres: Tensor | None = None)
 
 
 def _wgrad(dy: Tensor, x: Tensor, w: Tensor, grads: list, idx: int) -> None:
+    f2 = getattr(w, "_f2", None)
+    if f2 is not None:
+        w._f2_pending -= 1
+        if f2.enabled and w._f2_pending == 0:  # last contribution of this step: reduce-scatter + update
+            G.linear_wgrad_f2(dy, x, w.main_grad, f2)
+            return
     main = getattr(w, "main_grad", None)
     if main is not None:
         G.linear_wgrad_(dy, x, main)
@@ -66,13 +72,21 @@ class FusedPreNormBlock(torch.autograd.Function):
         hidden = w_o.shape[0]
         xn, r1, s = rmsnorm(x, eps, injection)
         sched = packed.schedule(causal)
-        gqkv = G.linear_rope(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden)
+        f1_qkv, f1_gu = getattr(w_gqkv, "_f1", None), getattr(w_gu, "_f1", None)
+        if f1_qkv is None:
+            gqkv = G.linear_rope(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden)
+        else:
+            gqkv = G.linear_rope_f1(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden, f1_qkv)
         o, y, lse = attention_fwd(gqkv, num_heads, sched)
         x1 = G.linear(y, w_o, residual=s)
         xn2, r2, _ = rmsnorm(x1, eps)
-        gu, h = G.linear_swiglu(xn2, w_gu)
+        gu, h = G.linear_swiglu(xn2, w_gu) if f1_gu is None else G.linear_swiglu_f1(xn2, w_gu, f1_gu)
         x2 = G.linear(h, w_d, residual=x1)
         if train:
+            for w in (w_gqkv, w_o, w_gu, w_d):
+                if getattr(w, "_f2", None) is not None:
+                    w._f2_pending += 1
+            ctx.weights = (w_gqkv, w_o, w_gu, w_d)
             ctx.save_for_backward(s, r1, xn, gqkv, o, lse, y, x1, r2, xn2, gu, h, w_gqkv, w_o, w_gu, w_d, cos, sin)
             ctx.packed, ctx.num_heads, ctx.causal = packed, num_heads, causal
             ctx.has_injection = injection is not None
@@ -80,7 +94,8 @@ class FusedPreNormBlock(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dx2):
-        (s, r1, xn, gqkv, o, lse, y, x1, r2, xn2, gu, h, w_gqkv, w_o, w_gu, w_d, cos, sin) = ctx.saved_tensors
+        (s, r1, xn, gqkv, o, lse, y, x1, r2, xn2, gu, h, _, _, _, _, cos, sin) = ctx.saved_tensors
+        w_gqkv, w_o, w_gu, w_d = ctx.weights  # the parameter objects (carry main_grad / F2 metadata)
         packed = ctx.packed
         dx2 = dx2.contiguous()
         grads = [None] * 4

@@ -110,3 +110,42 @@ def lm_head_ce_logits(x: Tensor, w: Tensor, labels: Tensor):
     _gemm(x, False, w, False, M, V, K, EPI_CE, logits, labels=labels, ce_max=pmax, ce_sum=psum, ce_arg=parg,
           ce_tgt=tgt)
     return logits, pmax, psum, parg, tgt
+
+
+# ---------------------------------------------------------------------------------------
+# fused-collective variants (multi-GPU sharding engine; see hrm_text_b200.parallel.fused)
+# ---------------------------------------------------------------------------------------
+def linear_rope_f1(x: Tensor, w: Tensor, positions: Tensor, cos: Tensor, sin: Tensor, rope_begin: int,
+                   rope_end: int, f1) -> Tensor:
+    """``linear_rope`` whose weight rows are gathered from their owners' shards in the same kernel."""
+    _check(x, w)
+    M, K = x.shape
+    N = w.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    cuda().gemm_f1(x, w, M, N, K, EPI_ROPE, out, None, positions, cos, sin, rope_begin, rope_end, 0, f1.maps,
+                   f1.shard_rows, f1.flags)
+    return out
+
+
+def linear_swiglu_f1(x: Tensor, w: Tensor, f1) -> tuple[Tensor, Tensor]:
+    """``linear_swiglu`` with the weight gathered from its owners' shards in the same kernel."""
+    _check(x, w)
+    M, K = x.shape
+    inter = w.shape[0] // 2
+    gu = torch.empty((M, 2 * inter), dtype=torch.bfloat16, device=x.device)
+    h = torch.empty((M, inter), dtype=torch.bfloat16, device=x.device)
+    cuda().gemm_f1(x, w, M, inter, K, EPI_SWIGLU, gu, h, None, None, None, 0, 0, inter, f1.maps, f1.shard_rows,
+                   f1.flags)
+    return gu, h
+
+
+def linear_wgrad_f2(dy: Tensor, x: Tensor, local_grad: Tensor, f2) -> None:
+    """Final weight-gradient GEMM of a step: ``local_grad + dy.T @ x`` is reduced into the
+    owners' shards and the owners' AdamATan2 update runs in the same kernel."""
+    _check(dy, x)
+    T, N = dy.shape
+    K = x.shape[1]
+    fc = f2.owner
+    base32, base16, hyper, b1, b2, wd, ema, has_m, has_ema = fc.f2_kernel_args()
+    cuda().gemm_f2(dy, x, N, K, T, local_grad, base32, base16, f2.offsets, f2.shard_rows, fc.params.shard_numel,
+                   fc.rank, fc.world, hyper, b1, b2, wd, ema, has_m, has_ema)

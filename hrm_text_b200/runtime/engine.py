@@ -24,6 +24,7 @@ On CPU (tests, gloo) the same engine runs the torch oracle path in fp32.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -72,7 +73,8 @@ class ShardedParameters:
     """Flat buffers for master shards, optimizer state, gradients and compute weights."""
 
     def __init__(self, model: nn.Module, *, beta1: float, beta2: float, weight_decay: float,
-                 ema: Optional[float], group=None, compute_dtype: Optional[torch.dtype] = None):
+                 ema: Optional[float], group=None, compute_dtype: Optional[torch.dtype] = None,
+                 fused: Optional[bool] = None):
         self.model = model
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -99,15 +101,31 @@ class ShardedParameters:
 
         dev = self.device
         f32 = dict(dtype=torch.float32, device=dev)
-        self.master = torch.zeros(self.shard_numel, **f32)
-        self.exp_avg = torch.zeros(self.shard_numel, **f32) if beta1 > 0 else None
-        self.exp_avg_sq = torch.zeros(self.shard_numel, **f32)
-        self.param_ema = torch.zeros(self.shard_numel, **f32) if ema is not None else None
-        self.grad = torch.zeros(self.full_numel, **f32)
-        self.grad_shard = self.grad if self.world == 1 else torch.zeros(self.shard_numel, **f32)
-        self.compute = torch.zeros(self.full_numel, dtype=self.compute_dtype, device=dev)
-        self.shard16 = None if self.world == 1 else torch.zeros(self.shard_numel, dtype=self.compute_dtype, device=dev)
         self.hyper = torch.zeros(4, **f32)  # lr, 1/bc1, 1/sqrt(bc2)
+        if fused is None:
+            fused = os.environ.get("HRM_FUSED_COLLECTIVES", "1") != "0"
+        self.fused = None
+        if fused and self.world > 1 and self.on_cuda:
+            # F1/F2: optimizer state, gradient shard and bf16 shards in peer-addressable memory
+            from ..parallel.fused import FusedCollectives
+            self.fused = FusedCollectives(self, group)
+            self.master = self.fused.view("master")
+            self.exp_avg = self.fused.view("exp_avg") if beta1 > 0 else None
+            self.exp_avg_sq = self.fused.view("exp_avg_sq")
+            self.param_ema = self.fused.view("param_ema") if ema is not None else None
+            self.grad_shard = self.fused.view("grad_shard")
+            self.shard16 = self.fused.buf16
+            self.grad = torch.zeros(self.full_numel, **f32)
+        else:
+            self.master = torch.zeros(self.shard_numel, **f32)
+            self.exp_avg = torch.zeros(self.shard_numel, **f32) if beta1 > 0 else None
+            self.exp_avg_sq = torch.zeros(self.shard_numel, **f32)
+            self.param_ema = torch.zeros(self.shard_numel, **f32) if ema is not None else None
+            self.grad = torch.zeros(self.full_numel, **f32)
+            self.grad_shard = self.grad if self.world == 1 else torch.zeros(self.shard_numel, **f32)
+            self.shard16 = None if self.world == 1 else torch.zeros(self.shard_numel, dtype=self.compute_dtype,
+                                                                    device=dev)
+        self.compute = torch.zeros(self.full_numel, dtype=self.compute_dtype, device=dev)
 
         with torch.no_grad():
             for s in self.slots:
@@ -138,10 +156,23 @@ class ShardedParameters:
             s.param.grad = None
             if self.on_cuda:
                 s.param.main_grad = self.full_view(self.grad, s)
+        if self.fused is not None:
+            self.fused.attach()
+
+    def _is_f1(self, s: ParamSlot) -> bool:
+        return self.fused is not None and s.fqn in self.fused.f1
+
+    def _is_f2(self, s: ParamSlot) -> bool:
+        return self.fused is not None and s.fqn in self.fused.f2
 
     # ------------------------------------------------------------------ step pieces
     def zero_grad(self) -> None:
         self.grad.zero_()
+        if self.fused is not None:
+            self.fused.reset_step()
+            for s in self.slots:
+                if self._is_f2(s):
+                    s.param._f2_pending = 0
         if not self.on_cuda:
             for s in self.slots:
                 s.param.grad = None
@@ -161,6 +192,8 @@ class ShardedParameters:
         if self.on_cuda:
             with dist._coalescing_manager(group=self.group, device=self.device):
                 for s in self.slots:
+                    if self._is_f2(s):
+                        continue  # reduced (and updated) inside the fused wgrad kernel
                     dist.reduce_scatter_tensor(self.grad_shard[s.shard_off: s.shard_off + s.shard_numel],
                                                self.full_padded_view(self.grad, s), op=dist.ReduceOp.SUM,
                                                group=self.group)
@@ -183,6 +216,18 @@ class ShardedParameters:
         self._host_hyper = host  # keep the pinned source alive until the copy is done
 
     def optimizer_step(self) -> None:
+        if self.on_cuda and self.fused is not None:
+            from .._native import cuda
+            for s in self.slots:
+                if self._is_f2(s):
+                    continue  # updated inside the fused wgrad kernel
+                sl = slice(s.shard_off, s.shard_off + s.shard_numel)
+                cuda().adam_atan2(self.master[sl], self.grad_shard[sl],
+                                  None if self.exp_avg is None else self.exp_avg[sl], self.exp_avg_sq[sl],
+                                  None if self.param_ema is None else self.param_ema[sl], self.shard16[sl],
+                                  self.hyper, self.beta1, self.beta2, self.weight_decay,
+                                  self.ema if self.ema is not None else 0.0)
+            return
         if self.on_cuda:
             from .._native import cuda
             out16 = self.compute if self.world == 1 else self.shard16
@@ -201,8 +246,12 @@ class ShardedParameters:
             else:
                 self.shard16.copy_(self.master)
 
-    def gather_params(self) -> None:
-        """Distribute the updated bf16 shards to every rank's resident compute buffer."""
+    def gather_params(self, all_slots: bool = False) -> None:
+        """Distribute the updated bf16 shards to every rank's resident compute buffer.
+
+        With fused collectives, F1 weights are gathered by their first GEMM of the next step
+        instead (unless ``all_slots``).
+        """
         if self.world == 1:
             if self.step_count == 0:  # initial fill
                 with torch.no_grad():
@@ -212,9 +261,12 @@ class ShardedParameters:
             return
         if self.step_count == 0:
             self.shard16.copy_(self.master)
+            all_slots = True
         if self.on_cuda:
             with dist._coalescing_manager(group=self.group, device=self.device):
                 for s in self.slots:
+                    if not all_slots and self._is_f1(s):
+                        continue
                     dist.all_gather_into_tensor(self.full_padded_view(self.compute, s),
                                                 self.shard16[s.shard_off: s.shard_off + s.shard_numel],
                                                 group=self.group)
@@ -253,10 +305,7 @@ class ShardedParameters:
                     self.full_view(self.compute, s).copy_(self.master_view(s).reshape(-1)[: s.numel].view(s.shape))
         else:
             self.shard16.copy_(self.master)
-            saved = self.step_count
-            self.step_count = max(1, saved)
-            self.gather_params()
-            self.step_count = saved
+            self.gather_params(all_slots=True)
 
 
 class TrainEngine:
@@ -316,16 +365,21 @@ class GraphedTrainStep:
     def capture(self, key, extra: dict) -> None:
         """Warm up eagerly (side stream), then capture one step body for ``extra`` kwargs."""
         eng = self.engine
+        fused = eng.params.fused
         self.stream.wait_stream(torch.cuda.current_stream())
+        if fused is not None:
+            fused.set_f2_enabled(False)  # warm-up must not apply optimizer updates
         with torch.cuda.stream(self.stream):
             for _ in range(self.warmup):
                 eng.forward_backward(self.static, **extra)
+        if fused is not None:
+            fused.set_f2_enabled(True)
         torch.cuda.current_stream().wait_stream(self.stream)
         torch.cuda.synchronize()
         torch.cuda.empty_cache()  # release warm-up activations before the graph pool grows
         eng.params.zero_grad()
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, pool=self.pool, stream=self.stream):
+        with torch.cuda.graph(g, pool=self.pool, stream=self.stream, capture_error_mode="relaxed"):
             out = eng.step_body(self.static, **extra)
         self.pool = g.pool()
         self.graphs[key] = g
