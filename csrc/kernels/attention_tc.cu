@@ -6,20 +6,23 @@
 // 128-query tiles, layout: 8 header ints then int4 {doc_start, len, prefix, q0} tiles).
 //
 // One CTA = one 128-query tile of one head, persistent over a static stride of the
-// LPT-sorted tile list. Warp roles (192 threads):
+// LPT-sorted tile list. Warp roles (320 threads):
 //   warp 0      TMA loads: Q tile once, K and V blocks of 128 keys through 2-stage rings
 //               (128B-swizzled [128 rows][64] boxes straight from the fused gqkv buffer)
 //   warp 1      UMMA issue (one lane): S_j = Q K_j^T into one of two TMEM S buffers, then
-//               O += P_{j-1} V_{j-1}, so S_j runs on the tensor cores while the softmax
-//               warps turn S_{j-1} into P_{j-1}
-//   warps 2..5  softmax, one query row per thread (TMEM lane quarter = warp % 4): reads S
-//               from TMEM twice (row max, then exp2), writes P (bf16) into a K-major
-//               swizzled shared-memory tile for the PV UMMA; keeps the running max m_used
-//               and sum l, and rescales the O row in TMEM only when the row max grows by
-//               more than 8 (log2 units) -- exact, since O and l share the stale max;
-//               finally normalises O, applies the gate and writes O, Y and LSE.
-// TMEM: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
-// Shared memory: Q 32 KB, K 2 x 32 KB, V 2 x 32 KB, P 32 KB.
+//               O_a += P_{j-1}[:, 0:64] V_{j-1}[0:64] and O_b += P_{j-1}[:, 64:128] V_{j-1}[64:128],
+//               so S_j runs on the tensor cores while the softmax warps turn S_{j-1} into P_{j-1}
+//   warps 2..5  softmax of key half 0 of every block, warps 6..9 of key half 1: one query row
+//   and 6..9    per thread (TMEM lane quarter = warp % 4), 64 scores read from TMEM once into
+//               registers. Each half keeps its own running max / sum and its own O
+//               accumulator, so the two warpgroups never synchronise inside the key loop;
+//               the two partial results are merged once per tile in the epilogue (the usual
+//               split-softmax combine). A half rescales its O accumulator in TMEM only when
+//               its row max grows by more than 8 (log2 units) -- exact, since O and l share
+//               the stale max. Two softmax warps per scheduler hide the TMEM/MUFU latency that
+//               one warp per scheduler cannot.
+// TMEM: S0 [0,128), S1 [128,256), O_a [256,384), O_b [384,512) (the whole 512 columns).
+// Shared memory: Q 32 KB, K 2 x 32 KB, V 2 x 32 KB, P 32 KB, per-row (max, sum) exchange 2 KB.
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error, drains its own
 // copies and UMMAs, frees TMEM and returns.
@@ -34,10 +37,11 @@ namespace attn_tc {
 
 constexpr int D = 128, BQ = 128, BKV = 128;
 constexpr int SCHED_HEADER = 8;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
 constexpr int TILE_BYTES = 128 * 128 * 2;  // one [128][128] bf16 tile = two [128][64] swizzled boxes
-constexpr int SMEM_BYTES = 1024 + 6 * TILE_BYTES + 512;
-constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_O = 256, TM_COLS = 512;
+constexpr int ML_BYTES = 2 * 128 * 8;      // per key half and row: (max, sum)
+constexpr int SMEM_BYTES = 1024 + 6 * TILE_BYTES + ML_BYTES + 512;
+constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_OA = 256, TM_OB = 384, TM_COLS = 512;
 constexpr float kRescaleThreshold = 8.0f;
 
 // mbarrier wait whose outcome is the same for every lane of the warp (the softmax warps run
@@ -85,7 +89,7 @@ struct Barriers {
   uint64_t q_full, q_empty;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2];
-  uint64_t p_full, o_done, o_free, drain;
+  uint64_t p_full[2], o_done[2], o_free, ml_full, drain;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -96,7 +100,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sK = smem + TILE_BYTES;          // 2 stages
   uint8_t* sV = smem + 3 * TILE_BYTES;      // 2 stages
   uint8_t* sP = smem + 5 * TILE_BYTES;
-  Barriers* bar = reinterpret_cast<Barriers*>(smem + 6 * TILE_BYTES);
+  float2* sML = reinterpret_cast<float2*>(smem + 6 * TILE_BYTES);
+  Barriers* bar = reinterpret_cast<Barriers*>(smem + 6 * TILE_BYTES + ML_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -113,11 +118,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bar->v_full[s], 1);
       mbar_init(&bar->v_empty[s], 1);
       mbar_init(&bar->s_full[s], 1);
-      mbar_init(&bar->s_free[s], 128);
+      mbar_init(&bar->s_free[s], 256);
+      mbar_init(&bar->p_full[s], 128);
+      mbar_init(&bar->o_done[s], 1);
     }
-    mbar_init(&bar->p_full, 128);
-    mbar_init(&bar->o_done, 1);
-    mbar_init(&bar->o_free, 128);
+    mbar_init(&bar->o_free, 256);
+    mbar_init(&bar->ml_full, 256);
     mbar_init(&bar->drain, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
@@ -191,20 +197,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         ok = false;
         return false;
       };
-      // O += P V for block `blk` (global block counter) of stage s; first block of an item overwrites O
+      // O_a += P[:, 0:64] V[0:64] and O_b += P[:, 64:128] V[64:128] for block `blk` (global
+      // block counter) of stage s, each as soon as its softmax half has written P; the first
+      // block of an item overwrites both accumulators
       auto issue_pv = [&](int blk, bool first) -> bool {
         const int s = blk & 1, r = blk >> 1;
-        if (!wait_or_fail(&bar->p_full, blk & 1, 21)) return false;
         if (!wait_or_fail(&bar->v_full[s], r & 1, 22)) return false;
-        tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // 16 keys per step
-          const uint64_t a = umma_desc_sw128(p_base + (k >> 2) * (TILE_BYTES / 2) + (k & 3) * 32, 16, 1024);
-          const uint64_t b = umma_desc_sw128(v_base + s * TILE_BYTES + k * 2048, TILE_BYTES / 2, 1024);
-          umma_f16_ss(tmem + TM_O, a, b, idesc_pv, (first && k == 0) ? 0u : 1u);
+        for (int g = 0; g < 2; ++g) {
+          if (!wait_or_fail(&bar->p_full[g], blk & 1, 21)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {  // 16 keys per step
+            const uint64_t a = umma_desc_sw128(p_base + g * (TILE_BYTES / 2) + k * 32, 16, 1024);
+            const uint64_t b = umma_desc_sw128(v_base + s * TILE_BYTES + (g * 4 + k) * 2048, TILE_BYTES / 2, 1024);
+            umma_f16_ss(tmem + (g ? TM_OB : TM_OA), a, b, idesc_pv, (first && k == 0) ? 0u : 1u);
+          }
+          if (g == 1) umma_commit(&bar->v_empty[s]);
+          umma_commit(&bar->o_done[g]);
         }
-        umma_commit(&bar->v_empty[s]);
-        umma_commit(&bar->o_done);
         return true;
       };
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
@@ -242,9 +253,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---------------------------------------------------------------- softmax / epilogue
+    const int wg = (warp - 2) >> 2;  // key half of every block handled by this warpgroup
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tm_o = tmem + lane_off + (wg ? TM_OB : TM_OA);
     const float sl = p.scale_log2;
     int n = 0, kv = 0;
     bool ok = true;
@@ -261,23 +274,36 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = kv & 1;
         if (!warp_wait(&bar->s_full[s], (kv >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 31); ok = false; break; }
         tc_fence_after();
-        const uint32_t ts = tmem + lane_off + (s ? TM_S1 : TM_S0);
-        const int k0 = j * BKV;
-        const bool masked = k0 + BKV > full_until;
-        // pass 1: block row max
-        float bmax = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(ts + c * 32, v);
+        float v[64];
+        {
+          uint32_t r0[32], r1[32];
+          const uint32_t ts = tmem + lane_off + (s ? TM_S1 : TM_S0) + wg * 64;
+          tmem_ld_32x32b_x32(ts, r0);
+          tmem_ld_32x32b_x32(ts + 32, r1);
+          tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const bool vis = !masked || (k0 + c * 32 + e < limit);
-            if (vis) bmax = fmaxf(bmax, v[e] * sl);
+            v[e] = __uint_as_float(r0[e]);
+            v[e + 32] = __uint_as_float(r1[e]);
           }
         }
-        // P_j overwrites P_{j-1}: wait for the previous PV (also guards the O rescale)
-        if (!warp_wait(&bar->o_done, (kv - 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 32); ok = false; break; }
+        tc_fence_before();
+        mbar_arrive(&bar->s_free[s]);  // S is in registers: the next QK^T may overwrite it
+        const int kbase = j * BKV + wg * 64;
+        if (kbase + 64 > full_until) {  // partially visible half-block (uniform per warpgroup)
+#pragma unroll
+          for (int e = 0; e < 64; ++e)
+            if (kbase + e >= limit) v[e] = -INFINITY;
+        }
+        float mx0 = v[0], mx1 = v[1];
+#pragma unroll
+        for (int e = 2; e < 64; e += 2) {
+          mx0 = fmaxf(mx0, v[e]);
+          mx1 = fmaxf(mx1, v[e + 1]);
+        }
+        const float bmax = fmaxf(mx0, mx1) * sl;  // scale > 0 commutes with max
+        // P_j overwrites this half of P_{j-1}: wait for its PV (also guards the O rescale)
+        if (!warp_wait(&bar->o_done[wg], (kv - 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 32); ok = false; break; }
         tc_fence_after();
         // The rescale decision is per row, but tcgen05.ld/st are warp-collective
         // (.sync.aligned): decide per warp, and let rows that need no rescale use alpha = 1.
@@ -288,11 +314,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
               uint32_t r[32];
-              tmem_ld_32x32b_x32(tmem + lane_off + TM_O + c * 32, r);
+              tmem_ld_32x32b_x32(tm_o + c * 32, r);
               tmem_ld_wait();
 #pragma unroll
               for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-              tmem_st_32x32b_x32(tmem + lane_off + TM_O + c * 32, r);
+              tmem_st_32x32b_x32(tm_o + c * 32, r);
             }
             tmem_st_wait();
           }
@@ -301,50 +327,65 @@ __global__ void __launch_bounds__(THREADS, 1)
             m_used = bmax;
           }
         }
-        // pass 2: P = exp2(s - m_used) -> bf16 K-major swizzled tile (row = query, 128B rows per 64 keys)
-        const float m_safe = m_used == -INFINITY ? 0.f : m_used;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(ts + c * 32, v);
-          uint32_t pk[16];
+        // P = exp2(s * scale - m_used) -> bf16 K-major swizzled box (row = query, 64 keys = 128 B)
+        const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+        uint8_t* prow = sP + wg * (TILE_BYTES / 2) + row * 128;
+        float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const bool vis0 = !masked || (k0 + c * 32 + e < limit);
-            const bool vis1 = !masked || (k0 + c * 32 + e + 1 < limit);
-            const float p0 = vis0 ? fast_exp2(v[e] * sl - m_safe) : 0.f;
-            const float p1 = vis1 ? fast_exp2(v[e + 1] * sl - m_safe) : 0.f;
-            l += p0 + p1;
-            pk[e >> 1] = pack_bf16x2(p0, p1);
-          }
-          uint8_t* prow = sP + (c >> 1) * (TILE_BYTES / 2) + row * 128;
+        for (int q = 0; q < 8; ++q) {
+          uint32_t pk[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int piece = (c & 1) * 4 + q;
-            *reinterpret_cast<uint4*>(prow + ((piece ^ (row & 7)) << 4)) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          for (int w = 0; w < 4; ++w) {
+            const int e = q * 8 + 2 * w;
+            const float p0 = fast_exp2(fmaf(v[e], sl, neg_m));
+            const float p1 = fast_exp2(fmaf(v[e + 1], sl, neg_m));
+            l0 += p0;
+            l1 += p1;
+            pk[w] = pack_bf16x2(p0, p1);
           }
+          *reinterpret_cast<uint4*>(prow + ((q ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
+        l += l0 + l1;
         fence_async_smem();
         tc_fence_before();
-        mbar_arrive(&bar->s_free[s]);
-        mbar_arrive(&bar->p_full);
+        mbar_arrive(&bar->p_full[wg]);
       }
       if (!ok) break;
-      // epilogue: wait for the last PV, normalise, gate, write O / Y / LSE
-      if (!warp_wait(&bar->o_done, (kv - 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 33); ok = false; break; }
+      // epilogue: wait for the last PV of both halves (O_b's commit follows O_a's), merge the
+      // two partial softmax results, normalise, gate, write this half's 64 columns of O / Y
+      if (!warp_wait(&bar->o_done[1], (kv - 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 33); ok = false; break; }
       tc_fence_after();
+      sML[wg * 128 + row] = make_float2(m_used, l);
+      mbar_arrive(&bar->ml_full);
+      if (!warp_wait(&bar->ml_full, n & 1)) { report_error(p.err, kErrAttnWaitTimeout, 34); ok = false; break; }
+      const float2 oth = sML[(wg ^ 1) * 128 + row];
+      const float m_all = fmaxf(m_used, oth.x);
+      const float m_ref = m_all == -INFINITY ? 0.f : m_all;
+      const float sc_me = fast_exp2(m_used - m_ref), sc_oth = fast_exp2(oth.x - m_ref);  // exp2(-inf) = 0
+      const float l_all = l * sc_me + oth.y * sc_oth;
+      const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
+      const float sa = (wg == 0 ? sc_me : sc_oth) * inv, sb = (wg == 0 ? sc_oth : sc_me) * inv;
       const bool row_ok = qi < len;
       const long tok = (long)doc_start + qi;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(tmem + lane_off + TM_O + c * 32, v);
+      for (int c = 0; c < 2; ++c) {
+        const int col = wg * 64 + c * 32;
+        float va[32], vb[32];
+        {
+          uint32_t ra[32], rb[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + TM_OA + col, ra);
+          tmem_ld_32x32b_x32(tmem + lane_off + TM_OB + col, rb);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            va[e] = __uint_as_float(ra[e]);
+            vb[e] = __uint_as_float(rb[e]);
+          }
+        }
         if (row_ok) {
-          __nv_bfloat16* orow = p.out + tok * p.ld_out + head * D + c * 32;
-          __nv_bfloat16* yrow = p.y + tok * p.ld_out + head * D + c * 32;
-          const uint4* grow = reinterpret_cast<const uint4*>(p.qkv + tok * p.ld_qkv + head * D + c * 32);
+          __nv_bfloat16* orow = p.out + tok * p.ld_out + head * D + col;
+          __nv_bfloat16* yrow = p.y + tok * p.ld_out + head * D + col;
+          const uint4* grow = reinterpret_cast<const uint4*>(p.qkv + tok * p.ld_qkv + head * D + col);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const uint4 gv = grow[q];
@@ -352,7 +393,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t ow[4], yw[4];
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
-              const float o0 = bf16_round(v[8 * q + 2 * w] * inv), o1 = bf16_round(v[8 * q + 2 * w + 1] * inv);
+              const int e = 8 * q + 2 * w;
+              const float o0 = bf16_round(va[e] * sa + vb[e] * sb);
+              const float o1 = bf16_round(va[e + 1] * sa + vb[e + 1] * sb);
               const float2 g = unpack_bf16x2(ga[w]);
               ow[w] = pack_bf16x2(o0, o1);
               yw[w] = pack_bf16x2(o0 * sigmoidf_(g.x), o1 * sigmoidf_(g.y));
@@ -362,7 +405,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      if (row_ok) p.lse[(long)head * p.T + tok] = m_used + __log2f(l);
+      if (wg == 0 && row_ok) p.lse[(long)head * p.T + tok] = m_all + __log2f(l_all);
       tc_fence_before();
       mbar_arrive(&bar->o_free);
     }
@@ -398,25 +441,34 @@ __global__ void zero_tail_kernel(__nv_bfloat16* out, __nv_bfloat16* y, long ld_o
 // =======================================================================================
 // Backward (tcgen05). One CTA = one 128-key block of one head (LPT-sorted key-block list),
 // looping over the 64-query blocks that can see those keys. Per query block b:
-//   S^T  = K Q^T      (M=128 keys, N=64 queries, K=128 dims)  -> TMEM
-//   dP^T = V dO^T     (same shape)                              -> TMEM
+//   S^T  = K Q^T      (M=128 keys, N=64 queries, K=128 dims)  -> TMEM region b % 2
+//   dP^T = V dO^T     (same shape)                              -> TMEM region b % 2
 //   softmax warps (row = key): P^T = exp2(S^T * scale_log2 - lse[q]) (masked to 0),
 //     dS^T = P^T * (dP^T - D[q]) * scale  -> bf16, K-major swizzled smem tiles
 //   dV  += P^T dO     (M=128 keys, N=128 dims, K=64 queries)   -> TMEM, whole key block
 //   dK  += dS^T Q     (same shape)                              -> TMEM, whole key block
-//   dQ^T = K^T dS^T   (M=128 dims, N=64 queries, K=128 keys)   -> TMEM; the dQ warps add it
-//     into the fp32 dQ accumulator (coalesced: a warp covers 32 consecutive dims of a query)
+//   dQ^T = K^T dS^T   (M=128 dims, N=64 queries, K=128 keys)   -> TMEM, in the S^T columns
+//     of region b % 2 (S^T of block b is already in the softmax warps' registers)
+// The UMMA warp issues S^T / dP^T of block b+1 before the dV / dK / dQ^T products of block b,
+// so the softmax of b+1 overlaps the tensor-core work of b (two TMEM regions).
+// The dQ warps move dQ^T from TMEM through a warp-private shared-memory tile and add it to the
+// fp32 dQ accumulator with bulk asynchronous reductions (cp.reduce.async.bulk .add.f32,
+// 128 contiguous bytes per query row and warp) instead of one atomic per element.
 // At the end of the key block the softmax warps apply the RoPE backward to dK and write the
 // dK / dV rows. Warp roles (320 threads): 0 TMA, 1 UMMA, 2-5 softmax + dK/dV epilogue, 6-9 dQ.
-// TMEM: S^T [0,64), dP^T [64,128), dQ^T [128,192), dV [256,384), dK [384,512).
-// Shared: K 32 KB, V 32 KB, Q 2x16 KB, dO 2x16 KB, P^T 16 KB, dS^T 16 KB, lse/D 2x512 B.
+// TMEM: S^T_0 [0,64), dP^T_0 [64,128), S^T_1 [128,192), dP^T_1 [192,256), dV [256,384),
+// dK [384,512).
+// Shared: K 32 KB, V 32 KB, Q 2x16 KB, dO 2x16 KB, P^T 16 KB, dS^T 16 KB, lse/D 2 KB,
+// dQ staging 4 x 8 KB.
 // =======================================================================================
 constexpr int BWD_THREADS = 320;
 constexpr int BQB = 64;                 // queries per block
 constexpr int QTILE_BYTES = BQB * 128 * 2;   // [64][128] bf16 = two [64][64] boxes (16 KB)
 constexpr int PTILE_BYTES = 128 * BQB * 2;   // [128 keys][64 queries] bf16 (16 KB)
-constexpr int BWD_SMEM_BYTES = 1024 + 2 * TILE_BYTES + 4 * QTILE_BYTES + 2 * PTILE_BYTES + 2048 + 512;
-constexpr uint32_t TB_S = 0, TB_DP = 64, TB_DQ = 128, TB_DV = 256, TB_DK = 384;
+constexpr int DQ_STAGE_BYTES = BQB * 32 * 4;  // per dQ warp: [64 queries][32 dims] fp32
+constexpr int BWD_SMEM_BYTES =
+    1024 + 2 * TILE_BYTES + 4 * QTILE_BYTES + 2 * PTILE_BYTES + 2048 + 4 * DQ_STAGE_BYTES + 512;
+constexpr uint32_t TB_S = 0, TB_DP = 64, TB_REGION = 128, TB_DV = 256, TB_DK = 384;
 
 struct BwdParams {
   __nv_bfloat16* dqkv;
@@ -437,8 +489,18 @@ struct BwdParams {
 struct BwdBarriers {
   uint64_t kv_full, kv_done, kv_free;
   uint64_t qd_full[2], qd_empty[2];
-  uint64_t s_full, s_free, p_full, p_free, dq_full, dq_free, drain;
+  uint64_t s_full[2], dq_full[2], dq_free[2];
+  uint64_t p_full, p_free, drain;
 };
+
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ int bwd_qstart(const int4& t) { return t.w < t.z ? 0 : t.w; }
 __device__ __forceinline__ int bwd_nqb(const int4& t) { return (t.y - bwd_qstart(t) + BQB - 1) / BQB; }
@@ -455,7 +517,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint8_t* sP = sDO + 2 * QTILE_BYTES;
   uint8_t* sDS = sP + PTILE_BYTES;
   float* sLse = reinterpret_cast<float*>(sDS + PTILE_BYTES);  // per softmax warp: [64] lse, [64] D
-  BwdBarriers* bar = reinterpret_cast<BwdBarriers*>(sLse + 512);
+  float* sDQ = sLse + 512;                                      // per dQ warp: [64][32] fp32
+  BwdBarriers* bar = reinterpret_cast<BwdBarriers*>(reinterpret_cast<uint8_t*>(sDQ) + 4 * DQ_STAGE_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -470,12 +533,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&bar->qd_full[s], 1);
       mbar_init(&bar->qd_empty[s], 1);
     }
-    mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->s_free, 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->s_full[s], 1);
+      mbar_init(&bar->dq_full[s], 1);
+      mbar_init(&bar->dq_free[s], 128);
+    }
     mbar_init(&bar->p_full, 128);
     mbar_init(&bar->p_free, 1);
-    mbar_init(&bar->dq_full, 1);
-    mbar_init(&bar->dq_free, 128);
     mbar_init(&bar->drain, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tm_kv);
@@ -545,6 +609,31 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         ok = false;
         return false;
       };
+      // dV, dK and dQ^T of block `bb` (global counter), stage / TMEM region bb % 2
+      auto finish = [&](int bb, bool first) -> bool {
+        const int s = bb & 1;
+        const uint32_t qs = qb0 + s * QTILE_BYTES, ds = db0 + s * QTILE_BYTES;
+        if (!wait_ok(&bar->p_full, bb & 1, 54)) return false;
+        if (first && !wait_ok(&bar->kv_free, (n & 1) ^ 1, 55)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // 16 queries per step
+          const uint64_t bo = umma_desc_sw128(ds + k * 2048, QTILE_BYTES / 2, 1024);
+          const uint64_t bq = umma_desc_sw128(qs + k * 2048, QTILE_BYTES / 2, 1024);
+          const uint32_t acc = (!first || k > 0) ? 1u : 0u;
+          umma_f16_ss(tmem + TB_DV, umma_desc_sw128(pb + k * 32, 16, 1024), bo, id_kv, acc);
+          umma_f16_ss(tmem + TB_DK, umma_desc_sw128(dsb + k * 32, 16, 1024), bq, id_kv, acc);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // 16 keys per step
+          umma_f16_ss(tmem + s * TB_REGION + TB_S, umma_desc_sw128(kb + k * 2048, TILE_BYTES / 2, 1024),
+                      umma_desc_sw128(dsb + k * 2048, PTILE_BYTES, 1024), id_dq, k > 0);
+        }
+        umma_commit(&bar->qd_empty[s]);
+        umma_commit(&bar->p_free);
+        umma_commit(&bar->dq_full[s]);
+        return true;
+      };
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
         const int4 t = tiles[item / p.H];
         const int nqb = bwd_nqb(t);
@@ -552,42 +641,26 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int qb = 0; qb < nqb; ++qb, ++b) {
           const int s = b & 1, r = b >> 1;
           if (!wait_ok(&bar->qd_full[s], r & 1, 52)) break;
-          if (!wait_ok(&bar->s_free, (b & 1) ^ 1, 53)) break;
+          // region s is free once the dQ warps have read dQ^T of block b - 2 (which implies
+          // the softmax warps consumed S^T / dP^T of b - 2 before it)
+          if (!wait_ok(&bar->dq_free[s], (r & 1) ^ 1, 53)) break;
           tc_fence_after();
           const uint32_t qs = qb0 + s * QTILE_BYTES, ds = db0 + s * QTILE_BYTES;
+          const uint32_t reg = tmem + s * TB_REGION;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {  // 16 dims per step
             const uint32_t oa = (k >> 2) * (TILE_BYTES / 2) + (k & 3) * 32;
             const uint32_t ob = (k >> 2) * (QTILE_BYTES / 2) + (k & 3) * 32;
-            umma_f16_ss(tmem + TB_S, umma_desc_sw128(kb + oa, 16, 1024), umma_desc_sw128(qs + ob, 16, 1024), id_s,
+            umma_f16_ss(reg + TB_S, umma_desc_sw128(kb + oa, 16, 1024), umma_desc_sw128(qs + ob, 16, 1024), id_s,
                         k > 0);
-            umma_f16_ss(tmem + TB_DP, umma_desc_sw128(vb + oa, 16, 1024), umma_desc_sw128(ds + ob, 16, 1024), id_s,
+            umma_f16_ss(reg + TB_DP, umma_desc_sw128(vb + oa, 16, 1024), umma_desc_sw128(ds + ob, 16, 1024), id_s,
                         k > 0);
           }
-          umma_commit(&bar->s_full);
-          if (!wait_ok(&bar->p_full, b & 1, 54)) break;
-          if (qb == 0 && !wait_ok(&bar->kv_free, (n & 1) ^ 1, 55)) break;
-          tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {  // 16 queries per step
-            const uint64_t bo = umma_desc_sw128(ds + k * 2048, QTILE_BYTES / 2, 1024);
-            const uint64_t bq = umma_desc_sw128(qs + k * 2048, QTILE_BYTES / 2, 1024);
-            const uint32_t acc = (qb > 0 || k > 0) ? 1u : 0u;
-            umma_f16_ss(tmem + TB_DV, umma_desc_sw128(pb + k * 32, 16, 1024), bo, id_kv, acc);
-            umma_f16_ss(tmem + TB_DK, umma_desc_sw128(dsb + k * 32, 16, 1024), bq, id_kv, acc);
-          }
-          if (!wait_ok(&bar->dq_free, (b & 1) ^ 1, 56)) break;
-          tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {  // 16 keys per step
-            umma_f16_ss(tmem + TB_DQ, umma_desc_sw128(kb + k * 2048, TILE_BYTES / 2, 1024),
-                        umma_desc_sw128(dsb + k * 2048, PTILE_BYTES, 1024), id_dq, k > 0);
-          }
-          umma_commit(&bar->qd_empty[s]);
-          umma_commit(&bar->p_free);
-          umma_commit(&bar->dq_full);
+          umma_commit(&bar->s_full[s]);
+          if (qb > 0 && !finish(b - 1, qb == 1)) break;
         }
         if (!ok) break;
+        if (!finish(b - 1, nqb == 1)) break;
         umma_commit(&bar->kv_done);
       }
       umma_commit(&bar->drain);
@@ -607,47 +680,88 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
       const int key = k0 + row;
       const bool key_ok = key < len;
+      // lse / D of the first query block; later blocks are prefetched one block ahead
+      float pre_l[2], pre_d[2];
+      auto fetch = [&](int qbase) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int q = qbase + lane + 32 * h;
+          const bool qv = q < len;
+          const long idx = (long)head * p.T + doc_start + q;
+          pre_l[h] = qv ? p.lse[idx] : 0.f;
+          pre_d[h] = qv ? p.dsum[idx] : 0.f;
+        }
+      };
+      fetch(qs);
+      float* lse_b = sLse + (warp - 2) * 2 * BQB;  // warp-private copy (no cross-warp barrier)
+      float* d_b = lse_b + BQB;
       for (int qb = 0; qb < nqb; ++qb, ++b) {
         const int qbase = qs + qb * BQB;  // doc-relative first query
-        // warp-private copy of this block's lse / D (no cross-warp barrier on this path)
-        float* lse_b = sLse + (warp - 2) * 2 * BQB;
-        float* d_b = lse_b + BQB;
         __syncwarp();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int j = lane + 32 * h;
-          const int q = qbase + j;
-          const bool qv = q < len;
-          const long idx = (long)head * p.T + doc_start + q;
-          lse_b[j] = qv ? p.lse[idx] : 0.f;
-          d_b[j] = qv ? p.dsum[idx] : 0.f;
+          lse_b[lane + 32 * h] = pre_l[h];
+          d_b[lane + 32 * h] = pre_d[h];
         }
         __syncwarp();
-        if (!warp_wait(&bar->s_full, b & 1)) { report_error(p.err, kErrAttnWaitTimeout, 61); ok = false; break; }
+        if (qb + 1 < nqb) fetch(qbase + BQB);  // consumed next iteration: latency overlaps this one
+        const int sreg = b & 1;
+        if (!warp_wait(&bar->s_full[sreg], (b >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 61); ok = false; break; }
         tc_fence_after();
+        float sv[64], dv[64];
+        {
+          uint32_t r0[32], r1[32];
+          const uint32_t reg = tmem + lo + sreg * TB_REGION;
+          tmem_ld_32x32b_x32(reg + TB_S, r0);
+          tmem_ld_32x32b_x32(reg + TB_S + 32, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            sv[e] = __uint_as_float(r0[e]);
+            sv[e + 32] = __uint_as_float(r1[e]);
+          }
+          tmem_ld_32x32b_x32(reg + TB_DP, r0);
+          tmem_ld_32x32b_x32(reg + TB_DP + 32, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            dv[e] = __uint_as_float(r0[e]);
+            dv[e + 32] = __uint_as_float(r1[e]);
+          }
+        }
+        // every (key, query) pair of the block visible: no per-element mask
+        const bool full = (k0 + 128 <= len) && (qbase + BQB <= len) && (k0 + 128 <= max(prefix, qbase + 1));
         uint32_t pp[32], dd[32];  // 64 bf16 each
+        if (full) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float sv[32], dv[32];
-          tmem_ld32(tmem + lo + TB_S + c * 32, sv);
-          tmem_ld32(tmem + lo + TB_DP + c * 32, dv);
+          for (int e = 0; e < 64; e += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(lse_b + e);
+            const float4 d4 = *reinterpret_cast<const float4*>(d_b + e);
+            const float p0 = fast_exp2(fmaf(sv[e], p.scale_log2, -l4.x));
+            const float p1 = fast_exp2(fmaf(sv[e + 1], p.scale_log2, -l4.y));
+            const float p2 = fast_exp2(fmaf(sv[e + 2], p.scale_log2, -l4.z));
+            const float p3 = fast_exp2(fmaf(sv[e + 3], p.scale_log2, -l4.w));
+            pp[e >> 1] = pack_bf16x2(p0, p1);
+            pp[(e >> 1) + 1] = pack_bf16x2(p2, p3);
+            dd[e >> 1] = pack_bf16x2(p0 * p.scale * (dv[e] - d4.x), p1 * p.scale * (dv[e + 1] - d4.y));
+            dd[(e >> 1) + 1] = pack_bf16x2(p2 * p.scale * (dv[e + 2] - d4.z), p3 * p.scale * (dv[e + 3] - d4.w));
+          }
+        } else {
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
+          for (int e = 0; e < 64; e += 2) {
             float pr[2], ds[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-              const int j = c * 32 + e + u;
+              const int j = e + u;
               const int q = qbase + j;
               const bool vis = key_ok && q < len && key < max(prefix, q + 1);
-              pr[u] = vis ? fast_exp2(sv[e + u] * p.scale_log2 - lse_b[j]) : 0.f;
-              ds[u] = pr[u] * (dv[e + u] - d_b[j]) * p.scale;
+              pr[u] = vis ? fast_exp2(fmaf(sv[j], p.scale_log2, -lse_b[j])) : 0.f;
+              ds[u] = pr[u] * p.scale * (dv[j] - d_b[j]);
             }
-            pp[c * 16 + (e >> 1)] = pack_bf16x2(pr[0], pr[1]);
-            dd[c * 16 + (e >> 1)] = pack_bf16x2(ds[0], ds[1]);
+            pp[e >> 1] = pack_bf16x2(pr[0], pr[1]);
+            dd[e >> 1] = pack_bf16x2(ds[0], ds[1]);
           }
         }
-        tc_fence_before();
-        mbar_arrive(&bar->s_free);
         if (!warp_wait(&bar->p_free, (b & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 62); ok = false; break; }
         uint8_t* prow = sP + row * 128;
         uint8_t* drow = sDS + row * 128;
@@ -660,6 +774,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
               make_uint4(dd[4 * piece], dd[4 * piece + 1], dd[4 * piece + 2], dd[4 * piece + 3]);
         }
         fence_async_smem();
+        tc_fence_before();
         mbar_arrive(&bar->p_full);
       }
       if (!ok) break;
@@ -707,8 +822,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   } else {
     // ---------------------------------------------------------------- dQ accumulation
     const int quarter = warp & 3;
-    const int dim = quarter * 32 + lane;  // TMEM lane = head dim
-    const uint32_t lo = (uint32_t)(quarter * 32) << 16;
+    const uint32_t lo = (uint32_t)(quarter * 32) << 16;  // TMEM lanes = head dims quarter*32..+32
+    float* stage = sDQ + (warp - 6) * (BQB * 32);        // [64 queries][32 dims]
     int b = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -716,24 +831,38 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const int head = item % p.H;
       const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
       for (int qb = 0; qb < nqb; ++qb, ++b) {
-        if (!warp_wait(&bar->dq_full, b & 1)) { report_error(p.err, kErrAttnWaitTimeout, 71); ok = false; break; }
+        const int sreg = b & 1;
+        if (!warp_wait(&bar->dq_full[sreg], (b >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 71); ok = false; break; }
         tc_fence_after();
-        const int qbase = qs + qb * BQB;
-        float* col = p.dq_acc + ((long)t.x + qbase) * (p.H * D) + head * D + dim;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tmem_ld32(tmem + lo + TB_DQ + c * 32, v);
+        uint32_t r0[32], r1[32];
+        const uint32_t reg = tmem + lo + sreg * TB_REGION + TB_S;
+        tmem_ld_32x32b_x32(reg, r0);
+        tmem_ld_32x32b_x32(reg + 32, r1);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&bar->dq_free[sreg]);  // TMEM region reusable: dQ^T is in registers
+        bulk_wait_group_read0();            // this lane's previous reductions have read the stage
+        __syncwarp();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int q = qbase + c * 32 + e;
-            if (q < t.y) atomicAdd(col + (long)(c * 32 + e) * (p.H * D), v[e]);
+        for (int e = 0; e < 32; ++e) {
+          stage[e * 32 + lane] = __uint_as_float(r0[e]);
+          stage[(e + 32) * 32 + lane] = __uint_as_float(r1[e]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        const int qbase = qs + qb * BQB;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int j = lane + 32 * h;
+          if (qbase + j < t.y) {
+            float* dst = p.dq_acc + ((long)t.x + qbase + j) * (p.H * D) + head * D + quarter * 32;
+            bulk_reduce_add_f32(dst, stage + j * 32, 128);
           }
         }
-        tc_fence_before();
-        mbar_arrive(&bar->dq_free);
+        bulk_commit_group();
       }
     }
+    bulk_wait_group0();
   }
 
   tc_fence_before();
