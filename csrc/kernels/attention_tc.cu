@@ -5,8 +5,8 @@
 // (head, token); zero rows for padding), same device-built work schedule (LPT-ordered
 // 128-query tiles, layout: 8 header ints then int4 {doc_start, len, prefix, q0} tiles).
 //
-// One CTA = one 128-query tile of one head, persistent over a static stride of the
-// LPT-sorted tile list. Warp roles (320 threads):
+// One CTA = one 128-query tile of one head at a time; persistent CTAs pull tiles of the
+// LPT-sorted list from a global counter (ItemRing below). Warp roles (320 threads):
 //   warp 0      TMA loads: Q tile once, K and V blocks of 128 keys through 2-stage rings
 //               (128B-swizzled [128 rows][64] boxes straight from the fused gqkv buffer)
 //   warp 1      UMMA issue (one lane): S_j = Q K_j^T into one of two TMEM S buffers, then
@@ -50,6 +50,58 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
 
+// Dynamic work distribution: the producer warp of each CTA pulls the next item of the
+// LPT-ordered list from a global counter and publishes it through a small shared-memory ring;
+// every other role of the CTA reads the same sequence. Greedy pulling over a cost-sorted list
+// keeps the CTAs' finishing times within about one item of each other (a static stride does
+// not: the most expensive items of every round land on the same CTAs).
+constexpr int kItemRing = 4;
+struct ItemRing {
+  uint64_t full[kItemRing], empty[kItemRing];
+  int item[kItemRing];
+};
+__device__ __forceinline__ void ring_init(ItemRing* r, int consumers) {
+  for (int i = 0; i < kItemRing; ++i) {
+    mbar_init(&r->full[i], 1);
+    mbar_init(&r->empty[i], consumers);
+  }
+}
+// producer (one thread): the k-th item of this CTA; false on a wait timeout
+__device__ __forceinline__ bool ring_push(ItemRing* r, int k, int* counter, int& item) {
+  const int s = k % kItemRing;
+  if (!mbar_wait(&r->empty[s], ((k / kItemRing) & 1) ^ 1)) return false;
+  item = atomicAdd(counter, 1);
+  *reinterpret_cast<volatile int*>(&r->item[s]) = item;
+  mbar_arrive(&r->full[s]);  // release: the slot's value is visible to the waiters
+  return true;
+}
+// consumer, one thread; INT_MAX on a wait timeout
+__device__ __forceinline__ int ring_pop_thread(ItemRing* r, int k) {
+  const int s = k % kItemRing;
+  if (!mbar_wait(&r->full[s], (k / kItemRing) & 1)) return INT_MAX;
+  const int it = *reinterpret_cast<volatile int*>(&r->item[s]);
+  mbar_arrive(&r->empty[s]);
+  return it;
+}
+// consumer, whole warp (same value in every lane); INT_MAX on a wait timeout
+__device__ __forceinline__ int ring_pop_warp(ItemRing* r, int k) {
+  const int s = k % kItemRing;
+  if (!__all_sync(0xffffffffu, mbar_wait(&r->full[s], (k / kItemRing) & 1))) return INT_MAX;
+  const int it = *reinterpret_cast<volatile int*>(&r->item[s]);
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&r->empty[s]);
+  return it;
+}
+// last CTA to finish resets the work counters, so one schedule serves every launch
+__device__ __forceinline__ void finish_items(int* counter, int* done) {
+  __threadfence();
+  if (atomicAdd(done, 1) == (int)gridDim.x - 1) {
+    *counter = 0;
+    *done = 0;
+    __threadfence();
+  }
+}
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -90,6 +142,7 @@ struct Barriers {
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2], o_done[2], o_free, ml_full, drain;
+  ItemRing ring;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -125,6 +178,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bar->o_free, 256);
     mbar_init(&bar->ml_full, 256);
     mbar_init(&bar->drain, 1);
+    ring_init(&bar->ring, 9);  // UMMA thread + 8 softmax warps
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
   }
@@ -150,7 +204,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       int n = 0, kv = 0;
       int last_q = -1, last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
       bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      for (int kk = 0; ok; ++kk, ++n) {
+        int item;
+        if (!ring_push(&bar->ring, kk, const_cast<int*>(p.sched) + 4, item)) { report_error(p.err, kErrAttnWaitTimeout, 10); ok = false; break; }
+        if (item >= n_items) break;
         const int4 t = tiles[item / p.H];
         const int head = item % p.H;
         const int qx = (p.H + head) * D, kx = (2 * p.H + head) * D, vx = (3 * p.H + head) * D;
@@ -218,7 +275,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         return true;
       };
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      for (int kk = 0; ok; ++kk, ++n) {
+        const int item = ring_pop_thread(&bar->ring, kk);
+        if (item == INT_MAX) { report_error(p.err, kErrAttnWaitTimeout, 9); ok = false; break; }
+        if (item >= n_items) break;
         const int4 t = tiles[item / p.H];
         const int nb = tile_blocks(t);
         if (!wait_or_fail(&bar->q_full, n & 1, 23)) break;
@@ -261,7 +321,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float sl = p.scale_log2;
     int n = 0, kv = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+    for (int kk = 0; ok; ++kk, ++n) {
+      const int item = ring_pop_warp(&bar->ring, kk);
+      if (item == INT_MAX) { report_error(p.err, kErrAttnWaitTimeout, 8); ok = false; break; }
+      if (item >= n_items) break;
       const int4 t = tiles[item / p.H];
       const int head = item % p.H;
       const int doc_start = t.x, len = t.y, prefix = t.z, q0 = t.w;
@@ -418,6 +481,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, TM_COLS);
   }
+  if (threadIdx.x == 0) finish_items(const_cast<int*>(p.sched) + 4, const_cast<int*>(p.sched) + 5);
 }
 
 // Zero O, Y and LSE of padding tokens [total, T).
@@ -439,8 +503,8 @@ __global__ void zero_tail_kernel(__nv_bfloat16* out, __nv_bfloat16* y, long ld_o
 
 
 // =======================================================================================
-// Backward (tcgen05). One CTA = one 128-key block of one head (LPT-sorted key-block list),
-// looping over the 64-query blocks that can see those keys. Per query block b:
+// Backward (tcgen05). One CTA = one 128-key block of one head at a time (pulled from the
+// LPT-sorted key-block list), looping over the 64-query blocks that can see those keys. Per query block b:
 //   S^T  = K Q^T      (M=128 keys, N=64 queries, K=128 dims)  -> TMEM region b % 2
 //   dP^T = V dO^T     (same shape)                              -> TMEM region b % 2
 //   softmax warps (row = key): P^T = exp2(S^T * scale_log2 - lse[q]) (masked to 0),
@@ -451,23 +515,26 @@ __global__ void zero_tail_kernel(__nv_bfloat16* out, __nv_bfloat16* y, long ld_o
 //     of region b % 2 (S^T of block b is already in the softmax warps' registers)
 // The UMMA warp issues S^T / dP^T of block b+1 before the dV / dK / dQ^T products of block b,
 // so the softmax of b+1 overlaps the tensor-core work of b (two TMEM regions).
-// The dQ warps move dQ^T from TMEM through a warp-private shared-memory tile and add it to the
-// fp32 dQ accumulator with bulk asynchronous reductions (cp.reduce.async.bulk .add.f32,
-// 128 contiguous bytes per query row and warp) instead of one atomic per element.
-// At the end of the key block the softmax warps apply the RoPE backward to dK and write the
-// dK / dV rows. Warp roles (320 threads): 0 TMA, 1 UMMA, 2-5 softmax + dK/dV epilogue, 6-9 dQ.
+// Warp roles (320 threads): 0 TMA, 1 UMMA, 2..9 compute. Compute warp group g (warps 2-5,
+// 6-9) owns queries [32g, 32g+32) of every block: the softmax of that half (two warps per
+// scheduler), then, after the next block's softmax, that half of dQ^T, which it moves from TMEM
+// through a warp-private shared-memory tile into the fp32 dQ accumulator with one tensor
+// reduction per warp and block (cp.reduce.async.bulk.tensor .add, a [32 x 32] fp32 box)
+// instead of one atomic per element. At the end of the key block group 0 applies
+// the RoPE backward to dK and writes it, group 1 writes dV.
 // TMEM: S^T_0 [0,64), dP^T_0 [64,128), S^T_1 [128,192), dP^T_1 [192,256), dV [256,384),
 // dK [384,512).
 // Shared: K 32 KB, V 32 KB, Q 2x16 KB, dO 2x16 KB, P^T 16 KB, dS^T 16 KB, lse/D 2 KB,
-// dQ staging 4 x 8 KB.
+// dQ staging 8 x 4 KB.
 // =======================================================================================
 constexpr int BWD_THREADS = 320;
 constexpr int BQB = 64;                 // queries per block
 constexpr int QTILE_BYTES = BQB * 128 * 2;   // [64][128] bf16 = two [64][64] boxes (16 KB)
 constexpr int PTILE_BYTES = 128 * BQB * 2;   // [128 keys][64 queries] bf16 (16 KB)
-constexpr int DQ_STAGE_BYTES = BQB * 32 * 4;  // per dQ warp: [64 queries][32 dims] fp32
-constexpr int BWD_SMEM_BYTES =
-    1024 + 2 * TILE_BYTES + 4 * QTILE_BYTES + 2 * PTILE_BYTES + 2048 + 4 * DQ_STAGE_BYTES + 512;
+constexpr int QSTAGES = 3;                   // Q / dO ring depth
+constexpr int DQ_STAGE_BYTES = 32 * 32 * 4;  // per compute warp: [32 queries][32 dims] fp32
+static_assert(8 * DQ_STAGE_BYTES == 2 * PTILE_BYTES, "dQ staging aliases the P^T / dS^T tiles");
+constexpr int BWD_SMEM_BYTES = 1024 + 2 * TILE_BYTES + 2 * QSTAGES * QTILE_BYTES + 2 * PTILE_BYTES + 2048 + 512;
 constexpr uint32_t TB_S = 0, TB_DP = 64, TB_REGION = 128, TB_DV = 256, TB_DK = 384;
 
 struct BwdParams {
@@ -484,18 +551,51 @@ struct BwdParams {
   const int* sched;
   int cap;
   int* err;
+  int profile;  // nonzero: accumulate per-phase clock counts into g_bwd_phase
+};
+
+// Phase tracing of the backward (off unless enabled from the host): cycles each role spends
+// in each wait / work phase, summed over CTAs, read by attn_bwd_phase_counters().
+constexpr int kBwdPhases = 20;
+__device__ unsigned long long g_bwd_phase[kBwdPhases];
+__device__ __forceinline__ unsigned long long cycle_clock() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+  return t;
+}
+struct PhaseClock {
+  bool on;
+  unsigned long long t, acc[kBwdPhases];
+  __device__ explicit PhaseClock(bool enabled) : on(enabled), t(enabled ? cycle_clock() : 0ull) {
+#pragma unroll
+    for (int i = 0; i < kBwdPhases; ++i) acc[i] = 0ull;
+  }
+  __device__ __forceinline__ void mark(int slot) {
+    if (on) {
+      const unsigned long long now = cycle_clock();
+      acc[slot] += now - t;
+      t = now;
+    }
+  }
+  __device__ __forceinline__ void flush(int lo, int hi) {
+    if (on)
+      for (int i = lo; i < hi; ++i) atomicAdd(&g_bwd_phase[i], acc[i]);
+  }
 };
 
 struct BwdBarriers {
   uint64_t kv_full, kv_done, kv_free;
-  uint64_t qd_full[2], qd_empty[2];
+  uint64_t qd_full[QSTAGES], qd_empty[QSTAGES];
   uint64_t s_full[2], dq_full[2], dq_free[2];
-  uint64_t p_full, p_free, drain;
+  uint64_t p_full, p_free, stage_free, drain;
+  ItemRing ring;
 };
 
-__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* smem_src, uint32_t bytes) {
-  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst),
-               "r"(smem_u32(smem_src)), "r"(bytes)
+// smem box -> global, element-wise fp32 add, through a tensor map (one instruction per box)
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(smem_src))
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -507,18 +607,22 @@ __device__ __forceinline__ int bwd_nqb(const int4& t) { return (t.y - bwd_qstart
 
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
-                       const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+                       const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_dq,
+                       const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = sK + TILE_BYTES;
-  uint8_t* sQ = sV + TILE_BYTES;               // 2 stages
-  uint8_t* sDO = sQ + 2 * QTILE_BYTES;         // 2 stages
-  uint8_t* sP = sDO + 2 * QTILE_BYTES;
+  uint8_t* sQ = sV + TILE_BYTES;               // QSTAGES stages
+  uint8_t* sDO = sQ + QSTAGES * QTILE_BYTES;   // QSTAGES stages
+  uint8_t* sP = sDO + QSTAGES * QTILE_BYTES;
   uint8_t* sDS = sP + PTILE_BYTES;
-  float* sLse = reinterpret_cast<float*>(sDS + PTILE_BYTES);  // per softmax warp: [64] lse, [64] D
-  float* sDQ = sLse + 512;                                      // per dQ warp: [64][32] fp32
-  BwdBarriers* bar = reinterpret_cast<BwdBarriers*>(reinterpret_cast<uint8_t*>(sDQ) + 4 * DQ_STAGE_BYTES);
+  float* sLse = reinterpret_cast<float*>(sDS + PTILE_BYTES);  // per compute warp: [32] lse, [32] D
+  // dQ staging, per compute warp [32][32] fp32, aliases the P^T / dS^T tiles: a block's dQ^T
+  // is drained after the UMMAs that read its P^T / dS^T completed, before the next block's
+  // P^T / dS^T are written
+  float* sDQ = reinterpret_cast<float*>(sP);
+  BwdBarriers* bar = reinterpret_cast<BwdBarriers*>(sLse + 512);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -528,23 +632,26 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bar->kv_full, 1);
     mbar_init(&bar->kv_done, 1);
-    mbar_init(&bar->kv_free, 128);
-    for (int s = 0; s < 2; ++s) {
+    mbar_init(&bar->kv_free, 256);
+    for (int s = 0; s < QSTAGES; ++s) {
       mbar_init(&bar->qd_full[s], 1);
       mbar_init(&bar->qd_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar->s_full[s], 1);
       mbar_init(&bar->dq_full[s], 1);
-      mbar_init(&bar->dq_free[s], 128);
+      mbar_init(&bar->dq_free[s], 256);
     }
-    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->p_full, 256);
     mbar_init(&bar->p_free, 1);
+    mbar_init(&bar->stage_free, 8);  // lane 0 of each compute warp
     mbar_init(&bar->drain, 1);
+    ring_init(&bar->ring, 9);  // UMMA thread + 8 compute warps
     fence_mbar_init();
     tma_prefetch_desc(&tm_kv);
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
   }
   if (warp == 1) {
     __syncwarp();
@@ -560,23 +667,39 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     // ---------------------------------------------------------------- TMA loads
     if (lane == 0) {
       int n = 0, qb_all = 0;
-      int last_kv = -1, last_q[2] = {-1, -1};
+      int last_kv = -1, last_q[QSTAGES] = {-1, -1, -1};
       bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      for (int kk = 0; ok; ++kk, ++n) {
+        int item;
+        if (!ring_push(&bar->ring, kk, const_cast<int*>(p.sched) + 6, item)) { report_error(p.err, kErrAttnWaitTimeout, 40); ok = false; break; }
+        if (item >= n_items) break;
         const int4 t = tiles[item / p.H];
         const int head = item % p.H;
         const int qx = (p.H + head) * D, kx = (2 * p.H + head) * D, vx = (3 * p.H + head) * D;
-        if (!mbar_wait(&bar->kv_done, (n & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 41); ok = false; break; }
-        mbar_arrive_expect_tx(&bar->kv_full, 2 * TILE_BYTES);
-        const int krow = t.x + t.w;
-        tma_load_2d(sK, &tm_kv, &bar->kv_full, kx, krow);
-        tma_load_2d(sK + TILE_BYTES / 2, &tm_kv, &bar->kv_full, kx + 64, krow);
-        tma_load_2d(sV, &tm_kv, &bar->kv_full, vx, krow);
-        tma_load_2d(sV + TILE_BYTES / 2, &tm_kv, &bar->kv_full, vx + 64, krow);
-        last_kv = n;
+        // K / V of this item can only land once the previous item's UMMAs are done with the
+        // single K / V buffer; its first QSTAGES query blocks can be loaded before that (their
+        // stages are freed by the previous item's blocks), so they are not held back by it.
+        bool kv_issued = false;
+        auto issue_kv = [&]() -> bool {
+          if (!mbar_wait(&bar->kv_done, (n & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 41); return false; }
+          mbar_arrive_expect_tx(&bar->kv_full, 2 * TILE_BYTES);
+          const int krow = t.x + t.w;
+          tma_load_2d(sK, &tm_kv, &bar->kv_full, kx, krow);
+          tma_load_2d(sK + TILE_BYTES / 2, &tm_kv, &bar->kv_full, kx + 64, krow);
+          tma_load_2d(sV, &tm_kv, &bar->kv_full, vx, krow);
+          tma_load_2d(sV + TILE_BYTES / 2, &tm_kv, &bar->kv_full, vx + 64, krow);
+          last_kv = n;
+          kv_issued = true;
+          return true;
+        };
         const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
         for (int qb = 0; qb < nqb; ++qb, ++qb_all) {
-          const int s = qb_all & 1, r = qb_all >> 1;
+          // block qb's stage was last used by block qb - QSTAGES: of this item if qb >= QSTAGES,
+          // which needs this item's K / V to have been issued
+          if (!kv_issued && (qb >= QSTAGES || mbar_try_wait(&bar->kv_done, (n & 1) ^ 1))) {
+            if (!issue_kv()) { ok = false; break; }
+          }
+          const int s = qb_all % QSTAGES, r = qb_all / QSTAGES;
           if (!mbar_wait(&bar->qd_empty[s], (r & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 42); ok = false; break; }
           mbar_arrive_expect_tx(&bar->qd_full[s], 2 * QTILE_BYTES);
           const int qrow = t.x + qs + qb * BQB;
@@ -586,10 +709,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           tma_load_2d(sDO + s * QTILE_BYTES + QTILE_BYTES / 2, &tm_do, &bar->qd_full[s], head * D + 64, qrow);
           last_q[s] = r;
         }
+        if (!ok) break;
+        if (!kv_issued && !issue_kv()) { ok = false; break; }
       }
       if (!ok) {
         if (last_kv >= 0) mbar_wait(&bar->kv_full, last_kv & 1);
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < QSTAGES; ++s)
           if (last_q[s] >= 0) mbar_wait(&bar->qd_full[s], last_q[s] & 1);
       }
     }
@@ -603,18 +728,22 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const uint32_t pb = smem_u32(sP), dsb = smem_u32(sDS);
       int n = 0, b = 0;
       bool ok = true;
+      PhaseClock pc(p.profile != 0);
       auto wait_ok = [&](uint64_t* x, uint32_t par, int site) {
         if (mbar_wait(x, par)) return true;
         report_error(p.err, kErrAttnWaitTimeout, site);
         ok = false;
         return false;
       };
-      // dV, dK and dQ^T of block `bb` (global counter), stage / TMEM region bb % 2
+      // dV, dK and dQ^T of block `bb` (global counter): Q / dO stage bb % QSTAGES, TMEM region bb % 2
       auto finish = [&](int bb, bool first) -> bool {
-        const int s = bb & 1;
-        const uint32_t qs = qb0 + s * QTILE_BYTES, ds = db0 + s * QTILE_BYTES;
+        const int s = bb & 1, qst = bb % QSTAGES;
+        const uint32_t qs = qb0 + qst * QTILE_BYTES, ds = db0 + qst * QTILE_BYTES;
+        pc.mark(13);
         if (!wait_ok(&bar->p_full, bb & 1, 54)) return false;
+        pc.mark(11);
         if (first && !wait_ok(&bar->kv_free, (n & 1) ^ 1, 55)) return false;
+        pc.mark(12);
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 4; ++k) {  // 16 queries per step
@@ -629,23 +758,30 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           umma_f16_ss(tmem + s * TB_REGION + TB_S, umma_desc_sw128(kb + k * 2048, TILE_BYTES / 2, 1024),
                       umma_desc_sw128(dsb + k * 2048, PTILE_BYTES, 1024), id_dq, k > 0);
         }
-        umma_commit(&bar->qd_empty[s]);
+        umma_commit(&bar->qd_empty[qst]);
         umma_commit(&bar->p_free);
         umma_commit(&bar->dq_full[s]);
         return true;
       };
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      for (int kk = 0; ok; ++kk, ++n) {
+        const int item = ring_pop_thread(&bar->ring, kk);
+        if (item == INT_MAX) { report_error(p.err, kErrAttnWaitTimeout, 9); ok = false; break; }
+        if (item >= n_items) break;
         const int4 t = tiles[item / p.H];
         const int nqb = bwd_nqb(t);
+        pc.mark(13);
         if (!wait_ok(&bar->kv_full, n & 1, 51)) break;
+        pc.mark(14);
         for (int qb = 0; qb < nqb; ++qb, ++b) {
-          const int s = b & 1, r = b >> 1;
-          if (!wait_ok(&bar->qd_full[s], r & 1, 52)) break;
-          // region s is free once the dQ warps have read dQ^T of block b - 2 (which implies
-          // the softmax warps consumed S^T / dP^T of b - 2 before it)
+          const int s = b & 1, r = b >> 1, qst = b % QSTAGES;
+          if (!wait_ok(&bar->qd_full[qst], (b / QSTAGES) & 1, 52)) break;
+          pc.mark(8);
+          // region s is free once dQ^T of block b - 2 has been read out of it (which implies
+          // S^T / dP^T of b - 2 were consumed before it)
           if (!wait_ok(&bar->dq_free[s], (r & 1) ^ 1, 53)) break;
+          pc.mark(9);
           tc_fence_after();
-          const uint32_t qs = qb0 + s * QTILE_BYTES, ds = db0 + s * QTILE_BYTES;
+          const uint32_t qs = qb0 + qst * QTILE_BYTES, ds = db0 + qst * QTILE_BYTES;
           const uint32_t reg = tmem + s * TB_REGION;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {  // 16 dims per step
@@ -657,212 +793,235 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                         k > 0);
           }
           umma_commit(&bar->s_full[s]);
+          pc.mark(10);
           if (qb > 0 && !finish(b - 1, qb == 1)) break;
         }
         if (!ok) break;
         if (!finish(b - 1, nqb == 1)) break;
         umma_commit(&bar->kv_done);
       }
+      pc.mark(13);
+      pc.flush(8, 15);
       umma_commit(&bar->drain);
       mbar_wait(&bar->drain, 0);
     }
-  } else if (warp < 6) {
-    // ---------------------------------------------------------------- softmax + dK/dV epilogue
+  } else {
+    // ------------------------------------------------ softmax, dQ and dK/dV epilogue (warps 2..9)
+    // Warp group g = 0 / 1 handles queries [32g, 32g+32) of every 64-query block: its softmax
+    // half (TMEM lanes = keys of this warp's quarter), then, once the UMMAs of that block are
+    // done, its half of dQ^T (TMEM lanes = head dims of this warp's quarter). At the end of a
+    // key block each group writes half of dK (RoPE backward) and half of dV.
+    const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // key within the block
+    const int row = quarter * 32 + lane;  // key within the block (softmax), head dim (dQ)
     const uint32_t lo = (uint32_t)(quarter * 32) << 16;
+    float* lse_b = sLse + (warp - 2) * 64;  // warp-private copy of this block's lse / D
+    float* d_b = lse_b + 32;
+    float* stage = sDQ + (warp - 2) * (32 * 32);  // dQ staging [32 queries][32 dims]
     int n = 0, b = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+    PhaseClock pc(p.profile != 0 && warp == 2);
+    // dQ^T of block bb (TMEM region bb % 2), queries qbase + [32g, 32g+32) of item tile t
+    auto drain_dq = [&](int bb, const int4& t, int head, int qbase) -> bool {
+      const int sreg = bb & 1;
+      pc.mark(7);
+      if (!warp_wait(&bar->dq_full[sreg], (bb >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 71); return false; }
+      pc.mark(4);
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem + lo + sreg * TB_REGION + TB_S + g * 32, r);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&bar->dq_free[sreg]);  // TMEM region reusable: dQ^T is in registers
+      if (lane == 0) bulk_wait_group_read0();  // the previous reduction has read the stage
+      __syncwarp();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) stage[e * 32 + lane] = __uint_as_float(r[e]);
+      fence_async_smem();
+      __syncwarp();
+      // one [32 queries][32 dims] fp32 box added into dQ; rows past the document receive the
+      // exact zeros of their masked dS (rows past T are clipped by the tensor map)
+      if (lane == 0) tma_reduce_add_2d(&tm_dq, stage, head * D + quarter * 32, t.x + qbase + g * 32);
+      if (lane == 0) bulk_commit_group();
+      pc.mark(5);
+      return true;
+    };
+    for (int kk = 0; ok; ++kk, ++n) {
+      const int item = ring_pop_warp(&bar->ring, kk);
+      pc.mark(18);
+      if (item == INT_MAX) { report_error(p.err, kErrAttnWaitTimeout, 8); ok = false; break; }
+      if (item >= n_items) break;
       const int4 t = tiles[item / p.H];
       const int head = item % p.H;
       const int doc_start = t.x, len = t.y, prefix = t.z, k0 = t.w;
       const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
       const int key = k0 + row;
       const bool key_ok = key < len;
-      // lse / D of the first query block; later blocks are prefetched one block ahead
-      float pre_l[2], pre_d[2];
+      const int pos_k = key_ok ? p.positions[(long)doc_start + key] : 0;  // for the dK RoPE backward
+      if (key_ok) {  // the rows are read at the end of the key block: have them in L2 by then
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.cos_tab + (long)pos_k * 64 + g * 32));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.sin_tab + (long)pos_k * 64 + g * 32));
+      }
+      // lse / D of this lane's query of the first block; later blocks one block ahead
+      float pre_l, pre_d;
       auto fetch = [&](int qbase) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int q = qbase + lane + 32 * h;
-          const bool qv = q < len;
-          const long idx = (long)head * p.T + doc_start + q;
-          pre_l[h] = qv ? p.lse[idx] : 0.f;
-          pre_d[h] = qv ? p.dsum[idx] : 0.f;
-        }
+        const int q = qbase + g * 32 + lane;
+        const bool qv = q < len;
+        const long idx = (long)head * p.T + doc_start + q;
+        pre_l = qv ? p.lse[idx] : 0.f;
+        pre_d = qv ? p.dsum[idx] : 0.f;
       };
       fetch(qs);
-      float* lse_b = sLse + (warp - 2) * 2 * BQB;  // warp-private copy (no cross-warp barrier)
-      float* d_b = lse_b + BQB;
       for (int qb = 0; qb < nqb; ++qb, ++b) {
-        const int qbase = qs + qb * BQB;  // doc-relative first query
+        const int qbase = qs + qb * BQB;  // doc-relative first query of the block
+        const int q0 = qbase + g * 32;    // first query of this warp's half
         __syncwarp();
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          lse_b[lane + 32 * h] = pre_l[h];
-          d_b[lane + 32 * h] = pre_d[h];
-        }
+        lse_b[lane] = pre_l;
+        d_b[lane] = pre_d;
         __syncwarp();
         if (qb + 1 < nqb) fetch(qbase + BQB);  // consumed next iteration: latency overlaps this one
         const int sreg = b & 1;
+        pc.mark(7);
         if (!warp_wait(&bar->s_full[sreg], (b >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 61); ok = false; break; }
+        pc.mark(0);
+        if (pc.on) pc.acc[15] += 1;
         tc_fence_after();
-        float sv[64], dv[64];
-        {
-          uint32_t r0[32], r1[32];
-          const uint32_t reg = tmem + lo + sreg * TB_REGION;
-          tmem_ld_32x32b_x32(reg + TB_S, r0);
-          tmem_ld_32x32b_x32(reg + TB_S + 32, r1);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            sv[e] = __uint_as_float(r0[e]);
-            sv[e + 32] = __uint_as_float(r1[e]);
-          }
-          tmem_ld_32x32b_x32(reg + TB_DP, r0);
-          tmem_ld_32x32b_x32(reg + TB_DP + 32, r1);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            dv[e] = __uint_as_float(r0[e]);
-            dv[e + 32] = __uint_as_float(r1[e]);
-          }
-        }
-        // every (key, query) pair of the block visible: no per-element mask
-        const bool full = (k0 + 128 <= len) && (qbase + BQB <= len) && (k0 + 128 <= max(prefix, qbase + 1));
-        uint32_t pp[32], dd[32];  // 64 bf16 each
+        uint32_t rs[32], rd[32];
+        const uint32_t reg = tmem + lo + sreg * TB_REGION + g * 32;
+        tmem_ld_32x32b_x32(reg + TB_S, rs);
+        tmem_ld_32x32b_x32(reg + TB_DP, rd);
+        tmem_ld_wait();
+        // every (key, query) pair of this half block visible: no per-element mask
+        const bool full = (k0 + 128 <= len) && (q0 + 32 <= len) && (k0 + 128 <= max(prefix, q0 + 1));
+        uint32_t pp[16], dd[16];
         if (full) {
 #pragma unroll
-          for (int e = 0; e < 64; e += 4) {
+          for (int e = 0; e < 32; e += 4) {
             const float4 l4 = *reinterpret_cast<const float4*>(lse_b + e);
             const float4 d4 = *reinterpret_cast<const float4*>(d_b + e);
-            const float p0 = fast_exp2(fmaf(sv[e], p.scale_log2, -l4.x));
-            const float p1 = fast_exp2(fmaf(sv[e + 1], p.scale_log2, -l4.y));
-            const float p2 = fast_exp2(fmaf(sv[e + 2], p.scale_log2, -l4.z));
-            const float p3 = fast_exp2(fmaf(sv[e + 3], p.scale_log2, -l4.w));
+            const float p0 = fast_exp2(fmaf(__uint_as_float(rs[e]), p.scale_log2, -l4.x));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(rs[e + 1]), p.scale_log2, -l4.y));
+            const float p2 = fast_exp2(fmaf(__uint_as_float(rs[e + 2]), p.scale_log2, -l4.z));
+            const float p3 = fast_exp2(fmaf(__uint_as_float(rs[e + 3]), p.scale_log2, -l4.w));
             pp[e >> 1] = pack_bf16x2(p0, p1);
             pp[(e >> 1) + 1] = pack_bf16x2(p2, p3);
-            dd[e >> 1] = pack_bf16x2(p0 * p.scale * (dv[e] - d4.x), p1 * p.scale * (dv[e + 1] - d4.y));
-            dd[(e >> 1) + 1] = pack_bf16x2(p2 * p.scale * (dv[e + 2] - d4.z), p3 * p.scale * (dv[e + 3] - d4.w));
+            dd[e >> 1] = pack_bf16x2(p0 * p.scale * (__uint_as_float(rd[e]) - d4.x),
+                                     p1 * p.scale * (__uint_as_float(rd[e + 1]) - d4.y));
+            dd[(e >> 1) + 1] = pack_bf16x2(p2 * p.scale * (__uint_as_float(rd[e + 2]) - d4.z),
+                                           p3 * p.scale * (__uint_as_float(rd[e + 3]) - d4.w));
           }
         } else {
 #pragma unroll
-          for (int e = 0; e < 64; e += 2) {
+          for (int e = 0; e < 32; e += 2) {
             float pr[2], ds[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int j = e + u;
-              const int q = qbase + j;
+              const int q = q0 + j;
               const bool vis = key_ok && q < len && key < max(prefix, q + 1);
-              pr[u] = vis ? fast_exp2(fmaf(sv[j], p.scale_log2, -lse_b[j])) : 0.f;
-              ds[u] = pr[u] * p.scale * (dv[j] - d_b[j]);
+              pr[u] = vis ? fast_exp2(fmaf(__uint_as_float(rs[j]), p.scale_log2, -lse_b[j])) : 0.f;
+              ds[u] = pr[u] * p.scale * (__uint_as_float(rd[j]) - d_b[j]);
             }
             pp[e >> 1] = pack_bf16x2(pr[0], pr[1]);
             dd[e >> 1] = pack_bf16x2(ds[0], ds[1]);
           }
         }
+        pc.mark(1);
         if (!warp_wait(&bar->p_free, (b & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 62); ok = false; break; }
+        pc.mark(2);
+        // the P^T / dS^T tiles of block b - 1 are consumed: drain dQ^T(b - 1) through them
+        if (qb > 0 && !drain_dq(b - 1, t, head, qbase - BQB)) { ok = false; break; }
+        // every compute warp's reduction has read its staging box before P^T / dS^T(b) land
+        if (lane == 0) {
+          bulk_wait_group_read0();
+          mbar_arrive(&bar->stage_free);
+        }
+        if (!warp_wait(&bar->stage_free, b & 1)) { report_error(p.err, kErrAttnWaitTimeout, 64); ok = false; break; }
+        pc.mark(7);
         uint8_t* prow = sP + row * 128;
         uint8_t* drow = sDS + row * 128;
 #pragma unroll
-        for (int piece = 0; piece < 8; ++piece) {
-          const int off = (piece ^ (row & 7)) << 4;
-          *reinterpret_cast<uint4*>(prow + off) =
-              make_uint4(pp[4 * piece], pp[4 * piece + 1], pp[4 * piece + 2], pp[4 * piece + 3]);
-          *reinterpret_cast<uint4*>(drow + off) =
-              make_uint4(dd[4 * piece], dd[4 * piece + 1], dd[4 * piece + 2], dd[4 * piece + 3]);
+        for (int i = 0; i < 4; ++i) {  // 16-byte pieces g*4 + i of the 128-byte swizzled row
+          const int off = ((g * 4 + i) ^ (row & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + off) = make_uint4(pp[4 * i], pp[4 * i + 1], pp[4 * i + 2], pp[4 * i + 3]);
+          *reinterpret_cast<uint4*>(drow + off) = make_uint4(dd[4 * i], dd[4 * i + 1], dd[4 * i + 2], dd[4 * i + 3]);
         }
         fence_async_smem();
         tc_fence_before();
         mbar_arrive(&bar->p_full);
+        pc.mark(3);
       }
       if (!ok) break;
-      // dK / dV of this key block: wait for its last MMAs, RoPE-backward dK, write both.
+      if (!drain_dq(b - 1, t, head, qs + (nqb - 1) * BQB)) { ok = false; break; }
+      pc.mark(7);
+      // dK (RoPE backward) and dV of this key block, split between the two groups
       if (!warp_wait(&bar->kv_done, n & 1)) { report_error(p.err, kErrAttnWaitTimeout, 63); ok = false; break; }
+      pc.mark(16);
       tc_fence_after();
       const long tok = (long)doc_start + key;
-      const int pos = key_ok ? p.positions[tok] : 0;
-      __nv_bfloat16* dk_row = p.dqkv + tok * p.ld_dqkv + (2 * p.H + head) * D;
-      __nv_bfloat16* dv_row = p.dqkv + tok * p.ld_dqkv + (3 * p.H + head) * D;
+      // group g: dK dims [32g, 32g+32) with their RoPE partners +64, and dV dims [64g, 64g+64);
+      // 16 dims per step with vector loads of cos / sin keep the loads in flight together
+      {
+        __nv_bfloat16* dk_row = p.dqkv + tok * p.ld_dqkv + (2 * p.H + head) * D;
+        __nv_bfloat16* dv_row = p.dqkv + tok * p.ld_dqkv + (3 * p.H + head) * D;
+        const float4* c4 = reinterpret_cast<const float4*>(p.cos_tab + (long)pos_k * 64 + g * 32);
+        const float4* s4 = reinterpret_cast<const float4*>(p.sin_tab + (long)pos_k * 64 + g * 32);
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {  // dims [c*32, c*32+32) pair with +64
-        float x1[32], x2[32], v1[32], v2[32];
-        tmem_ld32(tmem + lo + TB_DK + c * 32, x1);
-        tmem_ld32(tmem + lo + TB_DK + 64 + c * 32, x2);
-        tmem_ld32(tmem + lo + TB_DV + c * 32, v1);
-        tmem_ld32(tmem + lo + TB_DV + 64 + c * 32, v2);
-        if (key_ok) {
-          const float* cr = p.cos_tab + (long)pos * 64 + c * 32;
-          const float* sr = p.sin_tab + (long)pos * 64 + c * 32;
-          uint32_t a[16], bb[16], va[16], vb2[16];
+        for (int h = 0; h < 2; ++h) {
+          const int d0 = g * 32 + h * 16;
+          uint32_t r1[16], r2[16];
+          tmem_ld_32x32b_x16(tmem + lo + TB_DK + d0, r1);
+          tmem_ld_32x32b_x16(tmem + lo + TB_DK + 64 + d0, r2);
+          float cs[16], sn[16];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float c0 = cr[e], c1 = cr[e + 1], s0 = sr[e], s1 = sr[e + 1];
-            a[e >> 1] = pack_bf16x2(x1[e] * c0 + x2[e] * s0, x1[e + 1] * c1 + x2[e + 1] * s1);
-            bb[e >> 1] = pack_bf16x2(x2[e] * c0 - x1[e] * s0, x2[e + 1] * c1 - x1[e + 1] * s1);
-            va[e >> 1] = pack_bf16x2(v1[e], v1[e + 1]);
-            vb2[e >> 1] = pack_bf16x2(v2[e], v2[e + 1]);
+          for (int v = 0; v < 4; ++v) {
+            const float4 a = key_ok ? c4[h * 4 + v] : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 b = key_ok ? s4[h * 4 + v] : make_float4(0.f, 0.f, 0.f, 0.f);
+            cs[4 * v] = a.x; cs[4 * v + 1] = a.y; cs[4 * v + 2] = a.z; cs[4 * v + 3] = a.w;
+            sn[4 * v] = b.x; sn[4 * v + 1] = b.y; sn[4 * v + 2] = b.z; sn[4 * v + 3] = b.w;
           }
+          tmem_ld_wait();
+          if (key_ok) {
+            uint32_t a[8], bb[8];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            reinterpret_cast<uint4*>(dk_row + c * 32)[q] = make_uint4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]);
-            reinterpret_cast<uint4*>(dk_row + 64 + c * 32)[q] =
-                make_uint4(bb[4 * q], bb[4 * q + 1], bb[4 * q + 2], bb[4 * q + 3]);
-            reinterpret_cast<uint4*>(dv_row + c * 32)[q] =
-                make_uint4(va[4 * q], va[4 * q + 1], va[4 * q + 2], va[4 * q + 3]);
-            reinterpret_cast<uint4*>(dv_row + 64 + c * 32)[q] =
-                make_uint4(vb2[4 * q], vb2[4 * q + 1], vb2[4 * q + 2], vb2[4 * q + 3]);
+            for (int e = 0; e < 16; e += 2) {
+              const float x1a = __uint_as_float(r1[e]), x1b = __uint_as_float(r1[e + 1]);
+              const float x2a = __uint_as_float(r2[e]), x2b = __uint_as_float(r2[e + 1]);
+              a[e >> 1] = pack_bf16x2(x1a * cs[e] + x2a * sn[e], x1b * cs[e + 1] + x2b * sn[e + 1]);
+              bb[e >> 1] = pack_bf16x2(x2a * cs[e] - x1a * sn[e], x2b * cs[e + 1] - x1b * sn[e + 1]);
+            }
+            uint4* o1 = reinterpret_cast<uint4*>(dk_row + d0);
+            uint4* o2 = reinterpret_cast<uint4*>(dk_row + 64 + d0);
+            o1[0] = make_uint4(a[0], a[1], a[2], a[3]);
+            o1[1] = make_uint4(a[4], a[5], a[6], a[7]);
+            o2[0] = make_uint4(bb[0], bb[1], bb[2], bb[3]);
+            o2[1] = make_uint4(bb[4], bb[5], bb[6], bb[7]);
+          }
+        }
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          const int d0 = g * 64 + c * 32;
+          uint32_t rv[32];
+          tmem_ld_32x32b_x32(tmem + lo + TB_DV + d0, rv);
+          tmem_ld_wait();
+          if (key_ok) {
+            uint32_t va[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) va[e >> 1] = pack_bf16x2(__uint_as_float(rv[e]), __uint_as_float(rv[e + 1]));
+            uint4* o = reinterpret_cast<uint4*>(dv_row + d0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) o[q] = make_uint4(va[4 * q], va[4 * q + 1], va[4 * q + 2], va[4 * q + 3]);
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&bar->kv_free);
+      pc.mark(17);
     }
-  } else {
-    // ---------------------------------------------------------------- dQ accumulation
-    const int quarter = warp & 3;
-    const uint32_t lo = (uint32_t)(quarter * 32) << 16;  // TMEM lanes = head dims quarter*32..+32
-    float* stage = sDQ + (warp - 6) * (BQB * 32);        // [64 queries][32 dims]
-    int b = 0;
-    bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const int4 t = tiles[item / p.H];
-      const int head = item % p.H;
-      const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
-      for (int qb = 0; qb < nqb; ++qb, ++b) {
-        const int sreg = b & 1;
-        if (!warp_wait(&bar->dq_full[sreg], (b >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 71); ok = false; break; }
-        tc_fence_after();
-        uint32_t r0[32], r1[32];
-        const uint32_t reg = tmem + lo + sreg * TB_REGION + TB_S;
-        tmem_ld_32x32b_x32(reg, r0);
-        tmem_ld_32x32b_x32(reg + 32, r1);
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(&bar->dq_free[sreg]);  // TMEM region reusable: dQ^T is in registers
-        bulk_wait_group_read0();            // this lane's previous reductions have read the stage
-        __syncwarp();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          stage[e * 32 + lane] = __uint_as_float(r0[e]);
-          stage[(e + 32) * 32 + lane] = __uint_as_float(r1[e]);
-        }
-        fence_async_smem();
-        __syncwarp();
-        const int qbase = qs + qb * BQB;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int j = lane + 32 * h;
-          if (qbase + j < t.y) {
-            float* dst = p.dq_acc + ((long)t.x + qbase + j) * (p.H * D) + head * D + quarter * 32;
-            bulk_reduce_add_f32(dst, stage + j * 32, 128);
-          }
-        }
-        bulk_commit_group();
-      }
-    }
-    bulk_wait_group0();
+    if (lane == 0) bulk_wait_group0();
+    if (lane == 0) pc.flush(0, 8);
+    if (lane == 0) pc.flush(16, 20);
+    if (lane == 0 && pc.on) atomicAdd(&g_bwd_phase[15], pc.acc[15]);
   }
 
   tc_fence_before();
@@ -872,6 +1031,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, TM_COLS);
   }
+  if (threadIdx.x == 0) finish_items(const_cast<int*>(p.sched) + 6, const_cast<int*>(p.sched) + 7);
 }
 
 }  // namespace attn_tc
@@ -971,6 +1131,23 @@ static CUtensorMap make_map_rows(const at::Tensor& t, uint32_t box_rows) {
   return map;
 }
 
+static bool g_bwd_profile_enabled = false;
+
+// Phase tracing of the tcgen05 attention backward: enable / disable, and read (optionally
+// zeroing) the 16 per-phase cycle counters summed over CTAs (slot meanings in attention.py).
+void attn_bwd_set_profile(bool enabled) { g_bwd_profile_enabled = enabled; }
+at::Tensor attn_bwd_phase_counters(bool reset) {
+  unsigned long long host[attn_tc::kBwdPhases];
+  TORCH_CHECK(cudaMemcpyFromSymbol(host, attn_tc::g_bwd_phase, sizeof(host)) == cudaSuccess, "read phase counters");
+  if (reset) {
+    unsigned long long zero[attn_tc::kBwdPhases] = {};
+    TORCH_CHECK(cudaMemcpyToSymbol(attn_tc::g_bwd_phase, zero, sizeof(zero)) == cudaSuccess, "reset phase counters");
+  }
+  auto out = at::empty({attn_tc::kBwdPhases}, at::TensorOptions().dtype(at::kLong));
+  for (int i = 0; i < attn_tc::kBwdPhases; ++i) out[i] = (int64_t)host[i];
+  return out;
+}
+
 void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
                  const at::Tensor& lse, const at::Tensor& dy, const at::Tensor& positions, const at::Tensor& cos_tab,
                  const at::Tensor& sin_tab, const at::Tensor& d_out, const at::Tensor& dsum, const at::Tensor& dq_acc,
@@ -989,6 +1166,20 @@ void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   const CUtensorMap m_kv = make_map_rows(qkv, 128), m_q = make_map_rows(qkv, 64), m_do = make_map_rows(d_out, 64);
+  CUtensorMap m_dq;
+  {
+    TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous() && dq_acc.size(1) == H * attn_tc::D &&
+                    (reinterpret_cast<uintptr_t>(dq_acc.data_ptr()) & 15) == 0,
+                "dq_acc must be a contiguous fp32 [T, H*128] buffer");
+    cuuint64_t dims[2] = {(cuuint64_t)dq_acc.size(1), (cuuint64_t)dq_acc.size(0)};
+    cuuint64_t strides[1] = {(cuuint64_t)(dq_acc.stride(0) * 4)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn_attn()(&m_dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc.data_ptr(), dims, strides, box,
+                                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (dQ) failed: ", (int)r);
+  }
   attn_tc::BwdParams p{};
   p.dqkv = bfm(dqkv);
   p.ld_dqkv = dqkv.stride(0);
@@ -1005,6 +1196,7 @@ void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
   p.sched = sched.data_ptr<int>();
   p.cap = (int)((sched.numel() - attn_tc::SCHED_HEADER) / 8);
   p.err = device_error_word().data_ptr<int>();
+  p.profile = g_bwd_profile_enabled ? 1 : 0;
   static bool configured = false;
   if (!configured) {
     TORCH_CHECK(cudaFuncSetAttribute(attn_tc::attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1015,7 +1207,8 @@ void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
   int dev, sms;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  attn_tc::attn_bwd_tc_kernel<<<sms, attn_tc::BWD_THREADS, attn_tc::BWD_SMEM_BYTES, stream>>>(m_kv, m_q, m_do, p);
+  attn_tc::attn_bwd_tc_kernel<<<sms, attn_tc::BWD_THREADS, attn_tc::BWD_SMEM_BYTES, stream>>>(m_kv, m_q, m_do, m_dq,
+                                                                                               p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   attn::attn_bwd_post_kernel<<<1024, 256, 0, stream>>>(p.dq_acc, p.dqkv, p.ld_dqkv, p.positions, p.cos_tab, p.sin_tab, T,
                                                        (int)H, p.sched);

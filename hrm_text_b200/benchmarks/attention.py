@@ -34,6 +34,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--kernel", default="tcgen05", choices=["tcgen05", "mma"])
     ap.add_argument("--only", default="both", choices=["fwd", "bwd", "both"])
+    ap.add_argument("--phases", action="store_true", help="trace the backward's per-phase cycles (tcgen05)")
     args = ap.parse_args(argv)
 
     from ..data.synthetic import packed_batches
@@ -73,6 +74,11 @@ def main(argv=None):
         ms = timed(lambda: attention_bwd(qkv, H, sched, o, lse, dy, packed.position_ids, cos, sin))
         out["bwd_ms"] = ms
         out["bwd_tflops"] = 2.5 * fwd_flop / ms / 1e9
+        if args.phases and args.kernel == "tcgen05":
+            from ..ops.attention import bwd_phase_profile
+            ph = bwd_phase_profile(lambda: attention_bwd(qkv, H, sched, o, lse, dy, packed.position_ids, cos, sin))
+            blocks = max(1, ph.pop("query blocks"))
+            out["bwd_phase_cycles_per_query_block"] = {k: round(v / blocks, 1) for k, v in ph.items()}
     from ..utils.errors import check_device_errors
     check_device_errors()
     print(json.dumps(out))

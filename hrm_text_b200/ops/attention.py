@@ -96,6 +96,28 @@ def attention_bwd(gqkv: Tensor, num_heads: int, sched: Tensor, out: Tensor, lse:
     return dgqkv
 
 
+BWD_PHASES = ("wait S", "softmax math", "wait P free", "store P/dS", "wait dQ", "drain dQ", "dK/dV epilogue",
+              "other (compute warp)", "MMA wait Q/dO", "MMA wait dQ free", "MMA issue S/dP", "MMA wait P",
+              "MMA wait dK/dV free", "MMA issue dV/dK/dQ + other", "MMA wait K/V", "query blocks",
+              "epilogue wait dK/dV", "epilogue work", "item fetch", "unused")
+
+
+def bwd_phase_profile(fn) -> dict:
+    """Run ``fn`` with phase tracing of the tcgen05 backward enabled and return the cycles per
+    phase (one compute warp and the UMMA thread of every CTA, summed over CTAs) plus the number
+    of query blocks the traced warps processed."""
+    c = cuda()
+    c.attn_bwd_phase_counters(True)
+    c.attn_bwd_set_profile(True)
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        c.attn_bwd_set_profile(False)
+    vals = c.attn_bwd_phase_counters(True).tolist()
+    return dict(zip(BWD_PHASES, vals))
+
+
 class _VarlenPrefixLM(torch.autograd.Function):
     """Attention on separate (already rotated) q, k, v; used by the compatibility API."""
 
