@@ -218,6 +218,7 @@ def run_ours(args):
 
     launches_per_step = None if args.no_count else count_own_kernels(
         lambda: trainer.train_step_async(host_batches[0], lr=lr, bp_steps=bp))
+    fused = getattr(trainer.engine.params, "fused", None) is not None
     trainer.close()
 
     value = global_batch * args.steps / (device_ms / 1000.0)
@@ -230,7 +231,10 @@ def run_ours(args):
                     "prefix frac U[0,0.5], multipack LPT); random-init weights",
             "config": {"model": f"HRM-Text {args.size}", "global_batch": global_batch, "seq_len": MAX_SEQ_LEN,
                        "tokens_per_gpu": tokens_per_gpu, "bp_steps": bp, "parallelism": f"dp{world}",
-                       "sharding": "in-house dim-0 param/optimizer sharding, NCCL reduce-scatter/all-gather",
+                       "sharding": "in-house dim-0 param/optimizer sharding; " + (
+                           "block weights: all-gather fused into the QKV/gate-up GEMMs (F1), wgrad + reduce-scatter + "
+                           "AdamATan2 in one kernel (F2) over NVLink peer memory; embedding/head over NCCL"
+                           if fused else "NCCL reduce-scatter / all-gather"),
                        "l2": "inputs larger than L2 (per-step working set >> 126 MB)"},
             "clocks": clock_info, "e2e": e2e, "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
             "impl": "ours", "final_loss": last_loss,
