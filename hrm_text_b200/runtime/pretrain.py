@@ -32,6 +32,8 @@ from ..utils.logging import MetricLogger
 from . import checkpoint as ckpt
 from .factory import build_model, model_config_dict
 from .trainer import Trainer
+from .watchdog import Heartbeat, StepWatchdog
+from ..utils.errors import check_device_errors
 
 
 @dataclass
@@ -58,13 +60,15 @@ def init_distributed():
             torch.cuda.set_device(device)
         return 1, 0, 0, device
     local = int(os.environ["LOCAL_RANK"])
+    # collectives that wait longer than this fail instead of hanging (a rank that left the job)
+    timeout = timedelta(seconds=float(os.environ.get("HRM_PG_TIMEOUT_S", "1800")))
     if torch.cuda.is_available():
         device = torch.device("cuda", local)
         torch.cuda.set_device(device)
-        dist.init_process_group("nccl", device_id=device, timeout=timedelta(minutes=30))
+        dist.init_process_group("nccl", device_id=device, timeout=timeout)
     else:
         device = torch.device("cpu")
-        dist.init_process_group("gloo", timeout=timedelta(minutes=30))
+        dist.init_process_group("gloo", timeout=timeout)
     return dist.get_world_size(), dist.get_rank(), local, device
 
 
@@ -140,14 +144,32 @@ def run(config_name: str, overrides: list[str], max_steps: Optional[int] = None,
             ckpt.write_run_files(config.checkpoint_path, config.model_dump(), metadata.model_dump(),
                                  get_model_source_path(config.arch.name))
 
+    # Failure detection (off unless asked for): a per-step deadline that reports and
+    # interrupts a stuck rank, and a store heartbeat checked before each logging collective.
+    deadline = float(os.environ.get("HRM_STEP_DEADLINE_S", "0"))
+    watchdog = StepWatchdog(deadline) if deadline > 0 else None
+    heartbeat = None
+    if dist.is_initialized() and os.environ.get("HRM_HEARTBEAT", "0") == "1":
+        heartbeat = Heartbeat(dist.distributed_c10d._get_default_store(), rank, world)
+
     last, lr = {}, 0.0
     for epoch in range(1, config.epochs + 1):
         for batch, _info in loader:
             state.step += 1
             lr = lr_at(config, state.step, total_steps)
             extra = model.compute_train_extra_args(state)
+            if watchdog is not None:
+                watchdog.arm(state.step)
             _loss, metrics = trainer.train_step_async(batch, lr, extra.get("bp_steps"))
+            if heartbeat is not None:
+                heartbeat.set_step(state.step)
             if state.step % config.log_interval == 0:
+                if watchdog is not None and device.type == "cuda":
+                    check_device_errors()  # a device wait that gave up fails the step here
+                if heartbeat is not None:
+                    stale = heartbeat.stale_ranks(max_age_s=max(30.0, deadline))
+                    if stale:
+                        raise RuntimeError(f"ranks {stale} stopped heart-beating; aborting before the next collective")
                 reduced = reduce_metrics(metrics, "train/", rank)
                 if rank == 0:
                     last = reduced | extra | {"train/lr": lr}
@@ -159,6 +181,10 @@ def run(config_name: str, overrides: list[str], max_steps: Optional[int] = None,
         if max_steps is not None and state.step >= max_steps:
             break
 
+    if watchdog is not None:
+        watchdog.close()
+    if heartbeat is not None:
+        heartbeat.stop()
     trainer.close()
     logger.finish()
     if dist.is_initialized():
