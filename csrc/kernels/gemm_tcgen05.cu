@@ -64,6 +64,12 @@ constexpr int GEMM_SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) 
 constexpr int F2_STAGE_BYTES = EPI_WARPS * 32 * 32 * 4;
 template <int EPI>
 constexpr int gemm_smem_bytes() { return GEMM_SMEM_BYTES + (EPI == 7 ? F2_STAGE_BYTES : 0); }
+// CTA-pair (cta_group::2) variant: a 256 x 256 tile per pair of SMs, each SM stages its 128
+// rows of A and its 128 columns of B, so a k-block costs each SM 32 KB instead of 48 KB of
+// operand traffic for the same tensor-core work; 6 stages fit the same shared memory.
+constexpr int PAIR_STAGES = 6;
+constexpr int PAIR_SMEM_BYTES = 1024 + PAIR_STAGES * (A_STAGE_BYTES + B_STAGE_BYTES / 2) + 256;
+static_assert(PAIR_SMEM_BYTES <= 232448, "pair GEMM exceeds the shared-memory limit");
 static_assert(GEMM_SMEM_BYTES + F2_STAGE_BYTES <= 232448, "F2 GEMM exceeds the shared-memory limit");
 
 struct GemmArgs {
@@ -116,16 +122,16 @@ struct TileSched {
 // mode 0: whole tiles strided over CTAs; 1: stream-K (even split of all k-blocks over CTAs);
 // 2: fixed split-K (each tile in `split` equal k ranges, units strided over CTAs).
 template <typename F>
-__device__ __forceinline__ void for_each_segment(const TileSched& s, int mode, int split, F&& f) {
+__device__ __forceinline__ void for_each_segment(const TileSched& s, int mode, int split, int unit, int units, F&& f) {
   const int total_tiles = s.tiles();
   if (mode == 0) {
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+    for (int t = unit; t < total_tiles; t += units) {
       if (!f(t, 0, s.nk)) return;
     }
     return;
   }
   if (mode == 2) {
-    for (int u = blockIdx.x; u < total_tiles * split; u += gridDim.x) {
+    for (int u = unit; u < total_tiles * split; u += units) {
       const int t = u / split, q = u % split;
       const int kb0 = (int)((long long)s.nk * q / split), kb1 = (int)((long long)s.nk * (q + 1) / split);
       if (kb1 > kb0 && !f(t, kb0, kb1)) return;
@@ -133,8 +139,8 @@ __device__ __forceinline__ void for_each_segment(const TileSched& s, int mode, i
     return;
   }
   const long long total = (long long)total_tiles * s.nk;
-  const long long begin = total * blockIdx.x / gridDim.x;
-  const long long end = total * (blockIdx.x + 1) / gridDim.x;
+  const long long begin = total * unit / units;
+  const long long end = total * (unit + 1) / units;
   long long pos = begin;
   while (pos < end) {
     const int t = (int)(pos / s.nk);
@@ -226,39 +232,50 @@ __device__ __forceinline__ void tmem_load_f32x32(uint32_t taddr, float (&v)[32])
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-template <int A_MN, int B_MN, int EPI, int F1 = 0>
+template <int A_MN, int B_MN, int EPI, int F1 = 0, int PAIR = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
+  static_assert(!(PAIR && (F1 || EPI == EPI_F2)), "the fused-collective GEMMs run on single CTAs");
+  constexpr int kStages = PAIR ? PAIR_STAGES : STAGES;
+  constexpr int kBStage = PAIR ? B_STAGE_BYTES / 2 : B_STAGE_BYTES;
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE_BYTES);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint8_t* sB = smem + kStages * A_STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + kStages * kBStage);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* tfull_bar = empty_bar + kStages;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // CTA pairs: rank 0 issues the UMMAs for both; each CTA owns rows [cta_rank*128, +128) of
+  // the pair's 256-row tile. Work units are pairs.
+  const uint32_t cta_rank = PAIR ? cluster_cta_rank() : 0u;
+  const bool leader = cta_rank == 0;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   TileSched sched;
-  sched.m_tiles = (args.M + BM - 1) / BM;
+  sched.m_tiles = (args.M + TILE_M - 1) / TILE_M;
   sched.n_tiles = (EPI == EPI_SWIGLU) ? (args.N + 127) / 128 : (args.N + BN - 1) / BN;
   sched.nk = (args.K + BK - 1) / BK;
   const int mode = (EPI == EPI_F32ADD && args.stream_k) ? 1 : 0;
   const int split = 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 32 * EPI_WARPS);
+      // pairs: lane 0 of every epilogue warp of both CTAs arrives on the leader's barrier
+      mbar_init(&tempty_bar[a], PAIR ? 2 * EPI_WARPS : 32 * EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
@@ -267,11 +284,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // the peer's barriers are initialised
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -279,11 +302,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int it = 0;
-      int issued_round[STAGES];
+      int issued_round[kStages];
 #pragma unroll
-      for (int s = 0; s < STAGES; ++s) issued_round[s] = -1;
+      for (int s = 0; s < kStages; ++s) issued_round[s] = -1;
       bool ok = true;
-      for_each_segment(sched, mode, split, [&](int tile, int kb0, int kb1) -> bool {
+      for_each_segment(sched, mode, split, unit, units, [&](int tile, int kb0, int kb1) -> bool {
         const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
         // F1: tiles of the first M row read the weight from its owner's shard (peer memory,
         // plain TMA) and write it through to the local resident copy; other tiles wait for
@@ -298,15 +321,38 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           fence_proxy_async_global();
         }
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % STAGES, r = it / STAGES;
+          const int s = it % kStages, r = it / kStages;
           if (!mbar_wait(&empty_bar[s], (r & 1) ^ 1)) {
             report_error(args.err, kErrGemmWaitTimeout, 1);
             ok = false;
             return false;
           }
-          mbar_arrive_expect_tx(&full_bar[s], A_STAGE_BYTES + B_STAGE_BYTES);
           uint8_t* a_dst = sA + s * A_STAGE_BYTES;
-          uint8_t* b_dst = sB + s * B_STAGE_BYTES;
+          uint8_t* b_dst = sB + s * kBStage;
+          if constexpr (PAIR) {
+            // both CTAs' copies complete on the leader's barrier, which expects all of them
+            if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * (A_STAGE_BYTES + kBStage));
+            const uint32_t fb = cluster_map(&full_bar[s], 0);
+            const int row_a = mt * TILE_M + (int)cta_rank * BM;
+            if (!A_MN) {
+              tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, row_a);
+            } else {
+              tma_load_2d_pair(a_dst, &tmA, fb, row_a, kb * BK);
+              tma_load_2d_pair(a_dst + 8192, &tmA, fb, row_a + 64, kb * BK);
+            }
+            if (!B_MN) {  // this CTA's 128 columns of the tile: gate (rank 0) / up (rank 1) for SwiGLU
+              const int rb = (EPI == EPI_SWIGLU) ? (cta_rank ? args.pair_offset + nt * 128 : nt * 128)
+                                                 : nt * BN + (int)cta_rank * 128;
+              tma_load_2d_pair(b_dst, &tmB, fb, kb * BK, rb);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                tma_load_2d_pair(b_dst + j * 8192, &tmB, fb, nt * BN + ((int)cta_rank * 2 + j) * 64, kb * BK);
+            }
+            issued_round[s] = r;
+            continue;
+          }
+          mbar_arrive_expect_tx(&full_bar[s], A_STAGE_BYTES + B_STAGE_BYTES);
           if (!A_MN) {
             tma_load_2d(a_dst, &tmA, &full_bar[s], kb * BK, mt * BM);
           } else {
@@ -338,18 +384,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         return true;
       });
-      if (!ok) {
-        // Drain: wait (bounded) until every load this thread issued has landed.
-        for (int s = 0; s < STAGES; ++s)
+      if (!ok && !PAIR) {
+        // Drain: wait (bounded) until every load this thread issued has landed. (A pair's
+        // copies complete on the leader's barriers; the closing cluster barrier covers them.)
+        for (int s = 0; s < kStages; ++s)
           if (issued_round[s] >= 0) mbar_wait(&full_bar[s], issued_round[s] & 1);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ UMMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = umma_idesc_bf16(TILE_M, BN, A_MN, B_MN);
       int it = 0, local = 0;
-      for_each_segment(sched, mode, split, [&](int tile, int kb0, int kb1) -> bool {
+      for_each_segment(sched, mode, split, unit, units, [&](int tile, int kb0, int kb1) -> bool {
         const int acc = local & 1, use = local >> 1;
         if (!mbar_wait(&tempty_bar[acc], (use & 1) ^ 1)) {
           report_error(args.err, kErrGemmWaitTimeout, 2);
@@ -358,21 +405,28 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % STAGES, r = it / STAGES;
+          const int s = it % kStages, r = it / kStages;
           if (!mbar_wait(&full_bar[s], r & 1)) {
             report_error(args.err, kErrGemmWaitTimeout, 3);
             return false;
           }
           tc_fence_after();
           const uint32_t a_base = smem_u32(sA + s * A_STAGE_BYTES);
-          const uint32_t b_base = smem_u32(sB + s * B_STAGE_BYTES);
+          const uint32_t b_base = smem_u32(sB + s * kBStage);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t adesc = A_MN ? umma_desc_sw128(a_base + k * 2048, 8192, 1024)
                                         : umma_desc_sw128(a_base + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? umma_desc_sw128(b_base + k * 2048, 8192, 1024)
                                         : umma_desc_sw128(b_base + k * 32, 16, 1024);
-            umma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            else
+              umma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          if constexpr (PAIR) {
+            umma_commit_pair_mc(&empty_bar[s], 3);  // frees this stage in both CTAs
+            continue;
           }
           if (F1 && tile < sched.n_tiles) {  // first M row: write the gathered B boxes through
             const int nt = tile;
@@ -391,12 +445,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           fence_proxy_async_global();  // ... and visible to the TMA loads of other CTAs
           st_release_gpu(args.f1_flags + tile, 1);
         }
-        umma_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
+        if constexpr (PAIR)
+          umma_commit_pair_mc(&tfull_bar[acc], 3);  // both CTAs' accumulator halves ready
+        else
+          umma_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
         ++local;
         return true;
       });
       // Make sure every UMMA this thread issued has completed before TMEM is released.
-      umma_commit(drain_bar);
+      if constexpr (PAIR)
+        umma_commit_pair_mc(drain_bar, 1);
+      else
+        umma_commit(drain_bar);
       mbar_wait(drain_bar, 0);
     }
   } else {
@@ -405,7 +465,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int half = (warp - 2) >> 2;  // which column half of the tile this warp handles
     const int row = quarter * 32 + lane;
     int local = 0;
-    for_each_segment(sched, mode, split, [&](int tile, int kb0, int kb1) -> bool {
+    for_each_segment(sched, mode, split, unit, units, [&](int tile, int kb0, int kb1) -> bool {
       const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
       const int acc = local & 1, use = local >> 1;
       // warp-uniform outcome: the TMEM loads below are warp-collective
@@ -415,7 +475,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      const int m = mt * BM + row;
+      const int m = mt * TILE_M + (int)cta_rank * BM + row;
       const bool row_ok = m < args.M;
 
       if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
@@ -545,7 +605,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // and NVLink carries the fp32 gradient once, as a reduce-scatter would.
         // Each 32x32 chunk goes through the warp's smem tile (XOR-swizzled float4 slots) so
         // that every global access covers 4 rows x 128 contiguous bytes per instruction.
-        const int m0 = mt * BM;
+        const int m0 = mt * TILE_M + (int)cta_rank * BM;
         const int owner = m0 / args.f2_shard_rows;
         const long row0 = (long)(m0 - owner * args.f2_shard_rows) + quarter * 32;  // shard row of lane-row 0
         float* base = reinterpret_cast<float*>(args.f2_base32[owner]);
@@ -677,7 +737,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(cluster_map(&tempty_bar[acc], 0));
+      } else {
+        mbar_arrive(&tempty_bar[acc]);
+      }
       ++local;
       return true;
     });
@@ -685,10 +750,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  // pairs: the leader's UMMAs write the peer's TMEM and read its shared memory, and its commits
+  // arrive there: neither CTA releases TMEM or exits before both are done
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -740,6 +811,55 @@ int num_sms() {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   }
   return n;
+}
+
+// CTA pairs that can be resident at once (cluster placement can leave SMs unused).
+template <int A_MN, int B_MN, int EPI>
+int max_pair_clusters() {
+  static int n = 0;
+  if (n == 0) {
+    auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 0, 1>;
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES) ==
+                    cudaSuccess,
+                "cudaFuncSetAttribute failed");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.dynamicSmemBytes = PAIR_SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    TORCH_CHECK(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters > 0,
+                "no CTA pair of the GEMM fits on this device");
+    n = std::min(clusters, num_sms() / 2);
+  }
+  return n;
+}
+
+template <int A_MN, int B_MN, int EPI>
+void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int clusters,
+                 cudaStream_t stream) {
+  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 0, 1>;
+  max_pair_clusters<A_MN, B_MN, EPI>();  // sets the shared-memory attribute
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = PAIR_SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, args) == cudaSuccess, "pair GEMM launch failed");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <int A_MN, int B_MN, int EPI, int F1 = 0>
@@ -804,8 +924,35 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   const int64_t b_rows = b_mn ? K : b.size(0);
   CUtensorMap mb = b_mn ? make_map(b, N, K, b.stride(0), 64, 64) : make_map(b, K, b_rows, b.stride(0), 64, 128);
 
-  const int64_t m_tiles = (M + BM - 1) / BM;
   const int64_t n_tiles = (epi == EPI_SWIGLU) ? (N + 127) / 128 : (N + BN - 1) / BN;
+  // CTA pairs (256-row tiles) unless the problem is too short to fill them
+  static const bool pair_enabled = [] {
+    const char* v = std::getenv("HRM_GEMM_PAIR");
+    return v == nullptr || std::string(v) != "0";
+  }();
+  const bool pair = pair_enabled && M >= 1024;
+  if (pair) {
+    const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * n_tiles;
+#define HRM_GEMM_PAIR_CASE(AM, BMJ, E)                                                             \
+  if (a_mn == AM && b_mn == BMJ && epi == E) {                                                     \
+    const int cl = max_pair_clusters<AM, BMJ, E>();                                                \
+    const int clusters = (E == EPI_F32ADD && stream_k) ? cl : (int)std::min<int64_t>(tiles, cl);   \
+    return launch_pair<AM, BMJ, E>(ma, mb, args, clusters, stream);                                \
+  }
+    HRM_GEMM_PAIR_CASE(0, 0, EPI_STORE)
+    HRM_GEMM_PAIR_CASE(0, 0, EPI_RESIDUAL)
+    HRM_GEMM_PAIR_CASE(0, 0, EPI_ROPE)
+    HRM_GEMM_PAIR_CASE(0, 0, EPI_SWIGLU)
+    HRM_GEMM_PAIR_CASE(0, 0, EPI_CE)
+    HRM_GEMM_PAIR_CASE(0, 0, EPI_F32ADD)
+    HRM_GEMM_PAIR_CASE(0, 1, EPI_STORE)
+    HRM_GEMM_PAIR_CASE(0, 1, EPI_RESIDUAL)
+    HRM_GEMM_PAIR_CASE(0, 1, EPI_SWIGLU_BWD)
+    HRM_GEMM_PAIR_CASE(1, 1, EPI_F32ADD)
+    HRM_GEMM_PAIR_CASE(1, 1, EPI_STORE)
+#undef HRM_GEMM_PAIR_CASE
+  }
+  const int64_t m_tiles = (M + BM - 1) / BM;
   const int64_t tiles = m_tiles * n_tiles;
   int grid = (int)std::min<int64_t>(tiles, num_sms());
   if (epi == EPI_F32ADD && stream_k) grid = num_sms();
