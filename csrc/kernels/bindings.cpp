@@ -27,6 +27,8 @@ void attn_fwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const a
 void attn_fwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
                  const at::Tensor& y, const at::Tensor& lse);
 at::Tensor wait_flag_probe(const at::Tensor& flag, int64_t expected, double timeout_s);
+at::Tensor decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                            const at::Tensor& total);
 void attn_bwd_set_profile(bool enabled);
 at::Tensor attn_bwd_phase_counters(bool reset);
 void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
@@ -66,6 +68,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_tc", &hrm::attn_fwd_tc, "tcgen05 PrefixLM attention forward");
   m.def("attn_bwd", &hrm::attn_bwd);
   m.def("attn_bwd_tc", &hrm::attn_bwd_tc, "tcgen05 PrefixLM attention backward");
+  m.def("decode_attention", &hrm::decode_attention, "split-KV decode attention against a static KV cache");
   m.def("wait_flag_probe", &hrm::wait_flag_probe, "bounded device wait on a flag (failure-detection probe)");
   m.def("attn_bwd_set_profile", &hrm::attn_bwd_set_profile, "enable per-phase clock tracing of attn_bwd_tc");
   m.def("attn_bwd_phase_counters", &hrm::attn_bwd_phase_counters, "read (and optionally reset) the phase counters");

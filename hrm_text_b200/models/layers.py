@@ -182,6 +182,20 @@ def cached_attention_reference(q: Tensor, k: Tensor, v: Tensor, cache: Cache, ca
     return o.transpose(1, 2).to(q.dtype)
 
 
+def cached_attention(q: Tensor, k: Tensor, v: Tensor, cache: Cache, cache_lengths, is_causal: bool) -> Tensor:
+    """KV-cache attention: the sm_100a kernels for the decode step (one token per sequence)
+    and for a prompt prefilled into an empty cache; the torch reference for anything else
+    (CPU, other dtypes or head sizes, multi-token appends to a non-empty cache)."""
+    fast = q.is_cuda and q.shape[-1] == 128 and q.dtype == torch.bfloat16 and cache.keys.dtype == torch.bfloat16
+    if fast and q.shape[1] == 1 and not isinstance(cache_lengths, int):
+        from ..ops.decode import kv_decode
+        return kv_decode(q, k, v, cache, cache_lengths)
+    if fast and isinstance(cache_lengths, int) and cache_lengths == 0 and q.shape[0] == 1:
+        from ..ops.decode import kv_prefill
+        return kv_prefill(q, k, v, cache, is_causal)
+    return cached_attention_reference(q, k, v, cache, cache_lengths, is_causal)
+
+
 class Attention(nn.Module):
     def __init__(self, hidden_size: int, head_dim: int, num_heads: int, num_key_value_heads: int,
                  attn_type: str, init_std_in=None, init_std_out=None, **kwargs):
@@ -211,7 +225,7 @@ class Attention(nn.Module):
         if cache is None:
             attn = prefixlm_attention_reference(query, key, value, is_causal, prefix_lens, cu_seqlens)
         else:
-            attn = cached_attention_reference(query, key, value, cache, cache_lengths, is_causal)
+            attn = cached_attention(query, key, value, cache, cache_lengths, is_causal)
         gated = torch.sigmoid(gate.float()).to(attn.dtype) * attn
         return self.o_proj(gated.flatten(-2))
 
