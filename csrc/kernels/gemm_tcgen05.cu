@@ -69,7 +69,9 @@ constexpr int gemm_smem_bytes() { return GEMM_SMEM_BYTES + (EPI == 7 ? F2_STAGE_
 // operand traffic for the same tensor-core work; 6 stages fit the same shared memory.
 constexpr int PAIR_STAGES = 6;
 constexpr int PAIR_SMEM_BYTES = 1024 + PAIR_STAGES * (A_STAGE_BYTES + B_STAGE_BYTES / 2) + 256;
-static_assert(PAIR_SMEM_BYTES <= 232448, "pair GEMM exceeds the shared-memory limit");
+static_assert(PAIR_SMEM_BYTES + F2_STAGE_BYTES <= 232448, "pair GEMM exceeds the shared-memory limit");
+template <int EPI>
+constexpr int pair_smem_bytes() { return PAIR_SMEM_BYTES + (EPI == 7 ? F2_STAGE_BYTES : 0); }
 static_assert(GEMM_SMEM_BYTES + F2_STAGE_BYTES <= 232448, "F2 GEMM exceeds the shared-memory limit");
 
 struct GemmArgs {
@@ -236,7 +238,7 @@ template <int A_MN, int B_MN, int EPI, int F1 = 0, int PAIR = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
-  static_assert(!(PAIR && (F1 || EPI == EPI_F2)), "the fused-collective GEMMs run on single CTAs");
+  static_assert(!(PAIR && F1), "the fused all-gather GEMM runs on single CTAs");
   constexpr int kStages = PAIR ? PAIR_STAGES : STAGES;
   constexpr int kBStage = PAIR ? B_STAGE_BYTES / 2 : B_STAGE_BYTES;
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
@@ -610,7 +612,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const long row0 = (long)(m0 - owner * args.f2_shard_rows) + quarter * 32;  // shard row of lane-row 0
         float* base = reinterpret_cast<float*>(args.f2_base32[owner]);
         float* inbox = base + args.f2_grad_off;  // [src][shard]
-        int* cnt = reinterpret_cast<int*>(base + args.f2_cnt_off) + tile;
+        // one counter per 128-row half tile (identical numbering for single CTAs and pairs)
+        int* cnt = reinterpret_cast<int*>(base + args.f2_cnt_off) + (mt * (TILE_M / BM) + (int)cta_rank) * sched.n_tiles + nt;
         const float* local_grad = reinterpret_cast<const float*>(args.out);
         float* stg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full_bar) + 256) + (warp - 2) * 1024;
         const int rsub = lane >> 3, slot = lane & 7;
@@ -819,13 +822,13 @@ int max_pair_clusters() {
   static int n = 0;
   if (n == 0) {
     auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 0, 1>;
-    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES) ==
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem_bytes<EPI>()) ==
                     cudaSuccess,
                 "cudaFuncSetAttribute failed");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms() / 2));
     cfg.blockDim = dim3(GEMM_THREADS);
-    cfg.dynamicSmemBytes = PAIR_SMEM_BYTES;
+    cfg.dynamicSmemBytes = pair_smem_bytes<EPI>();
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -849,7 +852,7 @@ void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
   cfg.blockDim = dim3(GEMM_THREADS);
-  cfg.dynamicSmemBytes = PAIR_SMEM_BYTES;
+  cfg.dynamicSmemBytes = pair_smem_bytes<EPI>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1069,6 +1072,16 @@ void gemm_f2(const at::Tensor& dy, const at::Tensor& x, int64_t M, int64_t N, in
   args.f2_has_m = has_m ? 1 : 0; args.f2_has_ema = has_ema ? 1 : 0;
   CUtensorMap ma = make_map(dy, M, K, dy.stride(0), 64, 64);
   CUtensorMap mb = make_map(x, N, K, x.stride(0), 64, 64);
+  static const bool pair_enabled = [] {
+    const char* v = std::getenv("HRM_GEMM_PAIR");
+    return v == nullptr || std::string(v) != "0";
+  }();
+  if (pair_enabled && M >= 1024) {  // every rank computes the same launch shape (same tile order)
+    const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
+    const int clusters = (int)std::min<int64_t>(tiles, max_pair_clusters<1, 1, EPI_F2>());
+    launch_pair<1, 1, EPI_F2>(ma, mb, args, clusters, stream);
+    return;
+  }
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = (int)std::min<int64_t>(tiles, num_sms());
   launch<1, 1, EPI_F2>(ma, mb, args, grid, stream);

@@ -80,7 +80,9 @@ class FusedCollectives:
         # F2 inbox: one fp32 slot of the whole shard per source rank, [world][S]
         self.region["inbox"] = len(names) * S
 
-        f2_slots = [s for s in params.slots if s.fqn.endswith(F2_SUFFIXES) and s.chunk_rows % 128 == 0]
+        import os
+        enable_f2 = os.environ.get("HRM_F2", "1") != "0"  # HRM_F2=0: block-weight gradients over NCCL
+        f2_slots = [s for s in params.slots if enable_f2 and s.fqn.endswith(F2_SUFFIXES) and s.chunk_rows % 128 == 0]
         f1_slots = [s for s in params.slots if s.fqn.endswith(F1_SUFFIXES) and s.chunk_rows % 128 == 0]
         tiles = {s.fqn: (-(-s.rows // 128)) * (-(-s.cols // 256)) for s in f2_slots}
         cnt_total = sum(tiles.values())

@@ -103,7 +103,10 @@ class ShardedParameters:
         f32 = dict(dtype=torch.float32, device=dev)
         self.hyper = torch.zeros(4, **f32)  # lr, 1/bc1, 1/sqrt(bc2)
         if fused is None:
-            fused = os.environ.get("HRM_FUSED_COLLECTIVES", "1") != "0"
+            # F1/F2 fused collectives are opt-in: with CTA-pair GEMMs elsewhere, the plain NCCL
+            # path is faster end to end on one node (measured: 2 x B200, HRM-Text L, 300.0 ms
+            # vs 319.5 ms per step)
+            fused = os.environ.get("HRM_FUSED_COLLECTIVES", "0") == "1"
         self.fused = None
         if fused and self.world > 1 and self.on_cuda:
             # F1/F2: optimizer state, gradient shard and bf16 shards in peer-addressable memory
