@@ -86,8 +86,20 @@ def inference_load_checkpoint(ckpt_path: str, ckpt_epoch: Optional[int], ckpt_us
     return InferenceCheckpoint(model=model, carry=carry, tokenizer=tokenizer, tokenizer_info=meta.tokenizer_info)
 
 
+_SAMPLE_CALLS = [0]
+
+
 def sample(logits: Tensor, temp: float, generator: Optional[torch.Generator] = None) -> Tensor:
-    """Greedy for ``temp < 1e-5``; else Gumbel-max sampling at temperature ``temp``."""
+    """Greedy for ``temp < 1e-5``; else Gumbel-max sampling at temperature ``temp``.
+
+    On CUDA one fused kernel does the scaling, the Gumbel noise (counter-based, seeded from
+    ``generator`` or torch's default seed, advanced every call) and the argmax.
+    """
+    if logits.is_cuda and logits.dim() == 2 and logits.dtype in (torch.float32, torch.bfloat16):
+        from .._native import cuda
+        seed = generator.initial_seed() if generator is not None else torch.initial_seed()
+        _SAMPLE_CALLS[0] += 1
+        return cuda().sample_tokens(logits.contiguous(), float(temp), int(seed) & 0x7FFFFFFFFFFFFFFF, _SAMPLE_CALLS[0])
     if temp < 1e-5:
         return logits.argmax(-1)
     scaled = logits.float() / temp
