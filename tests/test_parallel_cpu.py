@@ -11,6 +11,7 @@ the SUM-reduced gradient is then 2x the single-rank one, which AdamATan2 ignores
 import os
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -89,11 +90,13 @@ def _rank_main(rank, world, out, port):
         dist.destroy_process_group()
 
 
-def test_two_gloo_ranks_match_one_rank(tmp_path):
-    out = str(tmp_path / "w2.pt")
-    mp.spawn(_rank_main, args=(2, out, 29681), nprocs=2, join=True)
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_match_one_rank(tmp_path, world):
+    """world 4 also exercises dim-0 chunks with padding (rows not divisible by the world)."""
+    out = str(tmp_path / f"w{world}.pt")
+    mp.spawn(_rank_main, args=(world, out, 29681 + world), nprocs=world, join=True)
     full2, losses2 = torch.load(out)
-    batches = [batch_from([packed_sequence(1000 * s), packed_sequence(1000 * s + 1)]) for s in range(STEPS)]
+    batches = [batch_from([packed_sequence(1000 * s + r) for r in range(world)]) for s in range(STEPS)]
     full1, losses1 = train(batches)
     assert all(np.isfinite(losses1)) and all(np.isfinite(losses2))
     # Elementwise agreement to fp32 summation noise; a few elements whose gradient nearly
