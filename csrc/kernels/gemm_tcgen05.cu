@@ -513,39 +513,53 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       } else if constexpr (EPI == EPI_ROPE) {
         // This warp handles frequency chunk c = half (columns [c*32, c*32+32) paired with +64)
-        // of both 128-wide heads of the tile; the cos/sin row slice is loaded once.
+        // of both 128-wide heads of the tile, 16 frequencies at a time (the cos / sin slices are
+        // re-read per head from L1) so the live registers stay under the 320-thread cap.
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
         const int c = half;
         const int pos = row_ok ? args.positions[m] : 0;
-        float cs[32], sn[32];
-        {
-          const float4* cr = reinterpret_cast<const float4*>(args.cos_tab + (long)pos * 64 + c * 32);
-          const float4* sr = reinterpret_cast<const float4*>(args.sin_tab + (long)pos * 64 + c * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 a = cr[q], b = sr[q];
-            cs[4 * q] = a.x; cs[4 * q + 1] = a.y; cs[4 * q + 2] = a.z; cs[4 * q + 3] = a.w;
-            sn[4 * q] = b.x; sn[4 * q + 1] = b.y; sn[4 * q + 2] = b.z; sn[4 * q + 3] = b.w;
-          }
-        }
+        const float4* cr = reinterpret_cast<const float4*>(args.cos_tab + (long)pos * 64 + c * 32);
+        const float4* sr = reinterpret_cast<const float4*>(args.sin_tab + (long)pos * 64 + c * 32);
 #pragma unroll 1
         for (int h = 0; h < 2; ++h) {
           const int head_col = nt * BN + h * 128;
           const bool rotate = head_col >= args.rope_begin && head_col < args.rope_end;
-          float x1[32], x2[32];
-          tmem_load_f32x32(taddr + h * 128 + c * 32, x1);
-          tmem_load_f32x32(taddr + h * 128 + 64 + c * 32, x2);
-          if (row_ok && head_col < args.N) {
-            if (rotate) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float a = x1[j], b = x2[j];
-                x1[j] = a * cs[j] - b * sn[j];
-                x2[j] = b * cs[j] + a * sn[j];
+          for (int sub = 0; sub < 2; ++sub) {
+            uint32_t r1[16], r2[16];
+            tmem_ld_32x32b_x16(taddr + h * 128 + c * 32 + sub * 16, r1);
+            tmem_ld_32x32b_x16(taddr + h * 128 + 64 + c * 32 + sub * 16, r2);
+            float cs[16], sn[16];
+            if (row_ok && rotate) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 a = cr[sub * 4 + q], b = sr[sub * 4 + q];
+                cs[4 * q] = a.x; cs[4 * q + 1] = a.y; cs[4 * q + 2] = a.z; cs[4 * q + 3] = a.w;
+                sn[4 * q] = b.x; sn[4 * q + 1] = b.y; sn[4 * q + 2] = b.z; sn[4 * q + 3] = b.w;
               }
             }
-            store_bf16x32(out + (long)m * args.ldo + head_col + c * 32, x1);
-            store_bf16x32(out + (long)m * args.ldo + head_col + 64 + c * 32, x2);
+            tmem_ld_wait();
+            if (row_ok && head_col < args.N) {
+              uint32_t o1[8], o2[8];
+#pragma unroll
+              for (int j = 0; j < 16; j += 2) {
+                float a0 = __uint_as_float(r1[j]), a1 = __uint_as_float(r1[j + 1]);
+                float b0 = __uint_as_float(r2[j]), b1 = __uint_as_float(r2[j + 1]);
+                if (rotate) {
+                  const float na0 = a0 * cs[j] - b0 * sn[j], na1 = a1 * cs[j + 1] - b1 * sn[j + 1];
+                  const float nb0 = b0 * cs[j] + a0 * sn[j], nb1 = b1 * cs[j + 1] + a1 * sn[j + 1];
+                  a0 = na0; a1 = na1; b0 = nb0; b1 = nb1;
+                }
+                o1[j >> 1] = pack_bf16x2(a0, a1);
+                o2[j >> 1] = pack_bf16x2(b0, b1);
+              }
+              uint4* d1 = reinterpret_cast<uint4*>(out + (long)m * args.ldo + head_col + c * 32 + sub * 16);
+              uint4* d2 = reinterpret_cast<uint4*>(out + (long)m * args.ldo + head_col + 64 + c * 32 + sub * 16);
+              d1[0] = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+              d1[1] = make_uint4(o1[4], o1[5], o1[6], o1[7]);
+              d2[0] = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+              d2[1] = make_uint4(o2[4], o2[5], o2[6], o2[7]);
+            }
           }
         }
       } else if constexpr (EPI == EPI_SWIGLU) {
@@ -564,7 +578,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             for (int j = 0; j < 32; ++j) {
               g[j] = bf16_round(g[j]);
               u[j] = bf16_round(u[j]);
-              hv[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+              hv[j] = __fdividef(g[j], 1.0f + __expf(-g[j])) * u[j];  // fast divide: output is bf16
             }
             store_bf16x32(gu + (long)m * args.ldo + f, g);
             store_bf16x32(gu + (long)m * args.ldo + args.pair_offset + f, u);
@@ -586,7 +600,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (ok) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float sg = 1.0f / (1.0f + __expf(-g[j]));
+              const float sg = __fdividef(1.0f, 1.0f + __expf(-g[j]));  // fast divide: outputs are bf16
               const float silu = g[j] * sg;
               const float dsilu = sg * (1.0f + g[j] * (1.0f - sg));
               const float d = bf16_round(dh[j]);
