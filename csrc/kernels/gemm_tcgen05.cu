@@ -99,6 +99,7 @@ struct GemmArgs {
   float* ce_tgt;
   int* err;
   int stream_k;
+  int splitk;  // EPI_F32ADD: > 1 selects K-chunk-major split-K instead of stream-K
   // F1: all-gather fused into the first GEMM that reads a sharded weight (B operand)
   const CUtensorMap* f1_peer_maps;  // [world] maps over each rank's bf16 shard of this weight
   int f1_shard_rows;                // rows per rank shard (a multiple of 128)
@@ -122,7 +123,7 @@ struct TileSched {
 
 // Iterate the (tile, kb0, kb1) segments this CTA owns; identical in every role.
 // mode 0: whole tiles strided over CTAs; 1: stream-K (even split of all k-blocks over CTAs);
-// 2: fixed split-K (each tile in `split` equal k ranges, units strided over CTAs).
+// 2: fixed split-K (each tile in `split` equal k ranges; units ordered K chunk first).
 template <typename F>
 __device__ __forceinline__ void for_each_segment(const TileSched& s, int mode, int split, int unit, int units, F&& f) {
   const int total_tiles = s.tiles();
@@ -133,8 +134,10 @@ __device__ __forceinline__ void for_each_segment(const TileSched& s, int mode, i
     return;
   }
   if (mode == 2) {
+    // K-chunk-major: the units running at the same time share one K chunk of both operands,
+    // so that chunk stays in L2 instead of every tile streaming all of K from DRAM
     for (int u = unit; u < total_tiles * split; u += units) {
-      const int t = u / split, q = u % split;
+      const int q = u / total_tiles, t = u % total_tiles;
       const int kb0 = (int)((long long)s.nk * q / split), kb1 = (int)((long long)s.nk * (q + 1) / split);
       if (kb1 > kb0 && !f(t, kb0, kb1)) return;
     }
@@ -266,8 +269,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   sched.m_tiles = (args.M + TILE_M - 1) / TILE_M;
   sched.n_tiles = (EPI == EPI_SWIGLU) ? (args.N + 127) / 128 : (args.N + BN - 1) / BN;
   sched.nk = (args.K + BK - 1) / BK;
-  const int mode = (EPI == EPI_F32ADD && args.stream_k) ? 1 : 0;
-  const int split = 1;
+  const int mode = (EPI == EPI_F32ADD && args.stream_k) ? (args.splitk > 1 ? 2 : 1) : 0;
+  const int split = (mode == 2) ? args.splitk : 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -936,6 +939,18 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   if (ce_tgt) args.ce_tgt = ce_tgt->data_ptr<float>();
   args.err = device_error_word().data_ptr<int>();
   args.stream_k = stream_k ? 1 : 0;
+  // fp32 weight gradients with a long K (tokens): split K into chunks whose operand slices
+  // (both [chunk, M] and [chunk, N] panels, ~48 MB) fit in L2 next to the accumulation traffic
+  args.splitk = 1;
+  if (epi == EPI_F32ADD && stream_k) {
+    const double panel_bytes = 2.0 * (double)K * (double)(M + N);
+    args.splitk = (int)std::min<double>(16.0, std::max(1.0, std::ceil(panel_bytes / (48.0 * 1024 * 1024))));
+    static const bool chunked = [] {
+      const char* v = std::getenv("HRM_WGRAD_SPLITK");
+      return v == nullptr || std::string(v) != "0";
+    }();
+    if (!chunked) args.splitk = 1;
+  }
 
   CUtensorMap ma = a_mn ? make_map(a, M, K, a.stride(0), 64, 64) : make_map(a, K, M, a.stride(0), 64, 128);
   const int64_t b_rows = b_mn ? K : b.size(0);
