@@ -696,26 +696,37 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) attn_bwd_kernel(const BwdParam
 // dq = RoPE^T(dq_acc) -> d(q) slice; zero dq/dk/dv slices of padding tokens.
 __global__ void attn_bwd_post_kernel(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, const int* positions,
                                      const float* cos_tab, const float* sin_tab, int T, int H, const int* sched) {
+  // 16 threads per (token, head) row, 4 rotation pairs (d, d + 64) each: 16-byte fp32 loads,
+  // 8-byte bf16 stores, no 64-bit division per element
   const int total = sched[2];
-  const long n = (long)T * H * 64;  // (token, head, pair)
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long tok = i / (H * 64);
-    const int rem = (int)(i % (H * 64));
-    const int head = rem / 64, d = rem % 64;
-    __nv_bfloat16* q_row = dqkv + tok * ld_dqkv + (H + head) * D;
-    if (tok >= total) {
-      q_row[d] = q_row[d + 64] = __float2bfloat16(0.f);
-      __nv_bfloat16* k_row = dqkv + tok * ld_dqkv + (2 * H + head) * D;
-      __nv_bfloat16* v_row = dqkv + tok * ld_dqkv + (3 * H + head) * D;
-      k_row[d] = k_row[d + 64] = v_row[d] = v_row[d + 64] = __float2bfloat16(0.f);
+  const int rows = T * H;
+  const int d = (threadIdx.x & 15) * 4;
+  const int stride = (int)((gridDim.x * blockDim.x) >> 4);
+  for (int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 4); r < rows; r += stride) {
+    const int tok = r / H, head = r - tok * H;
+    __nv_bfloat16* q_row = dqkv + (long)tok * ld_dqkv + (H + head) * D;
+    if (tok >= total) {  // padding tokens: zero dQ, dK, dV
+      const uint2 z = make_uint2(0u, 0u);
+      __nv_bfloat16* k_row = dqkv + (long)tok * ld_dqkv + (2 * H + head) * D;
+      __nv_bfloat16* v_row = dqkv + (long)tok * ld_dqkv + (3 * H + head) * D;
+      *reinterpret_cast<uint2*>(q_row + d) = z;
+      *reinterpret_cast<uint2*>(q_row + d + 64) = z;
+      *reinterpret_cast<uint2*>(k_row + d) = z;
+      *reinterpret_cast<uint2*>(k_row + d + 64) = z;
+      *reinterpret_cast<uint2*>(v_row + d) = z;
+      *reinterpret_cast<uint2*>(v_row + d + 64) = z;
       continue;
     }
-    const float* src = dq_acc + tok * (long)(H * D) + head * D;
-    const float a = src[d], b = src[d + 64];
+    const float* src = dq_acc + (long)tok * (H * D) + head * D;
+    const float4 a = *reinterpret_cast<const float4*>(src + d);
+    const float4 b = *reinterpret_cast<const float4*>(src + d + 64);
     const int pos = positions[tok];
-    const float c = cos_tab[pos * 64 + d], s = sin_tab[pos * 64 + d];
-    q_row[d] = __float2bfloat16(a * c + b * s);
-    q_row[d + 64] = __float2bfloat16(b * c - a * s);
+    const float4 c = *reinterpret_cast<const float4*>(cos_tab + (long)pos * 64 + d);
+    const float4 sn = *reinterpret_cast<const float4*>(sin_tab + (long)pos * 64 + d);
+    *reinterpret_cast<uint2*>(q_row + d) = make_uint2(pack_bf16x2(a.x * c.x + b.x * sn.x, a.y * c.y + b.y * sn.y),
+                                                      pack_bf16x2(a.z * c.z + b.z * sn.z, a.w * c.w + b.w * sn.w));
+    *reinterpret_cast<uint2*>(q_row + d + 64) = make_uint2(pack_bf16x2(b.x * c.x - a.x * sn.x, b.y * c.y - a.y * sn.y),
+                                                           pack_bf16x2(b.z * c.z - a.z * sn.z, b.w * c.w - a.w * sn.w));
   }
 }
 
