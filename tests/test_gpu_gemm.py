@@ -7,7 +7,10 @@ from gpu_utils import assert_close
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(256, 256, 128), (300, 512, 192), (1000, 1280, 1280), (128, 768, 64)]
+# M >= 1024 runs the CTA-pair kernel (256-row tiles; 1300 leaves a partial pair tile); the
+# last shape's weight gradient (K = 8192 tokens, 2048 x 2048) takes the K-chunk split-K path
+SHAPES = [(256, 256, 128), (300, 512, 192), (1000, 1280, 1280), (128, 768, 64), (1300, 768, 512),
+          (2048, 1280, 1280), (8192, 2048, 2048)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -35,11 +38,12 @@ def test_linear_dgrad_wgrad(cuda_device, M, N, K):
     assert_close(grad, 0.5 + dy.float().T @ x.float(), 1e-3, "wgrad accumulate")
 
 
-def test_linear_rope(cuda_device):
+@pytest.mark.parametrize("M", [384, 1300])
+def test_linear_rope(cuda_device, M):
     from hrm_text_b200.models.layers import apply_rotary_pos_emb, rope_tables
     from hrm_text_b200.ops import gemm as G
     torch.manual_seed(2)
-    M, H, K = 384, 2, 256
+    H, K = 2, 256
     N = 4 * H * 128
     x = torch.randn(M, K, device=cuda_device).bfloat16()
     w = torch.randn(N, K, device=cuda_device).bfloat16()
@@ -52,10 +56,11 @@ def test_linear_rope(cuda_device):
     assert_close(out, ref.view(M, N), 1e-2, "rope epilogue")
 
 
-def test_linear_swiglu_fwd_bwd(cuda_device):
+@pytest.mark.parametrize("M", [300, 1500])
+def test_linear_swiglu_fwd_bwd(cuda_device, M):
     from hrm_text_b200.ops import gemm as G
     torch.manual_seed(3)
-    M, K, I = 300, 256, 384
+    K, I = 256, 384
     x = torch.randn(M, K, device=cuda_device).bfloat16()
     w = (torch.randn(2 * I, K, device=cuda_device) / 16).bfloat16()
     gu, h = G.linear_swiglu(x, w)
@@ -72,10 +77,11 @@ def test_linear_swiglu_fwd_bwd(cuda_device):
     assert_close(dgu, torch.cat([gr.grad, ur.grad], -1), 2e-2, "swiglu bwd")
 
 
-def test_lm_head_cross_entropy(cuda_device):
+@pytest.mark.parametrize("T", [500, 1200])
+def test_lm_head_cross_entropy(cuda_device, T):
     from hrm_text_b200.ops.loss import lm_head_cross_entropy
     torch.manual_seed(4)
-    T, H, V = 500, 256, 2048
+    H, V = 256, 2048
     x = torch.randn(T, H, device=cuda_device).bfloat16().requires_grad_(True)
     w = (torch.randn(V, H, device=cuda_device) / 16).bfloat16().requires_grad_(True)
     labels = torch.randint(0, V, (T,), device=cuda_device, dtype=torch.int32)
