@@ -1,12 +1,19 @@
 """PrefixLM attention microbenchmark.
 
     python -m hrm_text_b200.benchmarks.attention [--heads 16] [--tokens 21504] [--iters 20]
-        [--kernel tcgen05|mma] [--only fwd|bwd|both]
+        [--kernel tcgen05|mma] [--only fwd|bwd|both] [--impl ours|reference]
 
 bf16, head_dim 128, ``tokens`` packed tokens (documents log-normal, median 512, clipped to
 [16, 4096], prefix fraction U[0, 0.5]), Q/K/V ~ N(0, 1) from seed 0. Each phase is timed
 with CUDA events over ``iters`` launches after warm-up; reported with its useful FLOPs
 (visible query-key pairs: 4 * pairs * 128 per head forward, 2.5x that backward).
+
+``--impl reference`` times the reference's own op on the same packing and inputs:
+``flash_attn_varlen_prefixlm`` from ``baseline/_ref/models/flash_attention_prefixlm_v2.py``
+(two varlen passes, bidirectional prefix then causal response, models/flash_attention_prefixlm_v2.py:88-131
+and :152-212) on the FlashAttention-2 stand-in for FA3 (``baseline/fa3_standin``). Its forward
+excludes the sigmoid gate that ours fuses, and its backward excludes the gate and RoPE backward
+that ours also does, so the comparison slightly favours the reference.
 """
 from __future__ import annotations
 
@@ -35,6 +42,7 @@ def main(argv=None):
     ap.add_argument("--kernel", default="tcgen05", choices=["tcgen05", "mma"])
     ap.add_argument("--only", default="both", choices=["fwd", "bwd", "both"])
     ap.add_argument("--phases", action="store_true", help="trace the backward's per-phase cycles (tcgen05)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     args = ap.parse_args(argv)
 
     from ..data.synthetic import packed_batches
@@ -64,6 +72,12 @@ def main(argv=None):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / args.iters
 
+    if args.impl == "reference":
+        out.update(_reference_times(qkv, H, b, s, dev, timed, fwd_flop, args.only))
+        out["kernel"] = "reference flash_attn_varlen_prefixlm on the FA3 stand-in"
+        print(json.dumps(out))
+        return
+
     o, y, lse = attention_fwd(qkv, H, sched, kernel=args.kernel)
     if args.only in ("fwd", "both"):
         ms = timed(lambda: attention_fwd(qkv, H, sched, kernel=args.kernel))
@@ -82,6 +96,43 @@ def main(argv=None):
     from ..utils.errors import check_device_errors
     check_device_errors()
     print(json.dumps(out))
+
+
+def _reference_times(qkv, H, b, s, dev, timed, fwd_flop, only) -> dict:
+    """Forward / backward times of the reference's PrefixLM op on the same packed batch."""
+    import os
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    ref = os.path.join(root, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref, "models", "flash_attention_prefixlm_v2.py")):
+        return {"unavailable": "baseline/_ref is missing"}
+    sys.path.insert(0, os.path.join(root, "baseline", "fa3_standin"))
+    sys.path.insert(0, ref)
+    from models.flash_attention_prefixlm_v2 import flash_attn_varlen_prefixlm
+    T = qkv.shape[0]
+    w = H * 128
+    q, k, v = (qkv[:, (i + 1) * w:(i + 2) * w].reshape(T, H, 128).contiguous().requires_grad_(True)
+               for i in range(3))
+    dtensors = {key: b[key].to(dev) for key in ("prefix_lens", "causal_lens", "cu_seqlens")}
+    scalars = [torch.tensor(s[key]) for key in ("total_seqlen", "numseqs", "max_seqlen_prefix",
+                                                "max_seqlen_causal", "max_seqlen_all")]
+
+    def fwd():
+        return flash_attn_varlen_prefixlm(q, k, v, False, dtensors["prefix_lens"], dtensors["causal_lens"],
+                                          dtensors["cu_seqlens"], *scalars)
+    res = {}
+    if only in ("fwd", "both"):
+        with torch.no_grad():
+            ms = timed(fwd)
+        res["fwd_ms"] = ms
+        res["fwd_tflops"] = fwd_flop / ms / 1e9
+    if only in ("bwd", "both"):
+        o = fwd()
+        dy = torch.randn(T, H, 128, device=dev).bfloat16()
+        ms = timed(lambda: torch.autograd.grad(o, (q, k, v), dy, retain_graph=True))
+        res["bwd_ms"] = ms
+        res["bwd_tflops"] = 2.5 * fwd_flop / ms / 1e9
+    return res
 
 
 if __name__ == "__main__":

@@ -10,16 +10,18 @@ Behaviour (reference models/baselines/hrm_nocarry_bp_warmup.py):
   them, L the rest (:78-81);
 * ``bp_steps`` ramps linearly from ``bp_min_steps`` to ``bp_max_steps`` over the first
   ``bp_warmup_ratio`` of training (:93-97).
+
+The recurrence is expressed as a call plan (``recurrence.hierarchical_plan``) that the shared
+driver in ``recurrence.py`` runs.
 """
 from __future__ import annotations
 
 from typing import Any, Optional
 
-import torch
 from torch import Tensor, nn
 
-from ..common import trunc_normal_init_
 from ..transformer import Transformer, TransformerConfig
+from .recurrence import ModuleCall, PlannedRecurrence, hierarchical_plan, init_state_vector
 
 
 class HierarchicalReasoningModelConfig(TransformerConfig):
@@ -59,7 +61,10 @@ def bp_steps_schedule(step: int, total_steps: int, warmup_ratio: float, lo: int,
     return lo + int(progress * (hi - lo))
 
 
-class HierarchicalReasoningModel(nn.Module):
+class HierarchicalReasoningModel(PlannedRecurrence):
+    output_state = "H"
+    plan_kwargs = ("bp_steps",)
+
     def __init__(self, config_dict: dict) -> None:
         super().__init__()
         config = HierarchicalReasoningModelConfig(**config_dict)
@@ -77,39 +82,16 @@ class HierarchicalReasoningModel(nn.Module):
         self.bp_min_steps, self.bp_max_steps = config.bp_min_steps, config.bp_max_steps
         self.hidden_size = config.hidden_size
         self.head_hint = self.H_level.core.head_hint
+        self.zL_init = init_state_vector(config.hidden_size)
 
-        self.zL_init = nn.Buffer(trunc_normal_init_(torch.empty(config.hidden_size, dtype=torch.bfloat16), std=1.0),
-                                 persistent=True)
-
-    def create_cache(self, **kwargs):
-        return dict(H=[self.H_level.create_cache(**kwargs) for _ in range(self.H_cycles)],
-                    L=[self.L_level.create_cache(**kwargs) for _ in range(self.H_cycles * self.L_cycles)])
-
-    def call_plan(self, bp_steps: int) -> list[tuple[str, int, bool]]:
-        """The module calls of one forward in order: ``(level, cache index, grad enabled)``."""
+    def call_plan(self, bp_steps: int = 2) -> list[ModuleCall]:
+        """The module calls of one forward, in order (``bp_steps`` of them record gradients)."""
         h_bp, l_bp = split_bp_steps(bp_steps, self.H_cycles)
-        plan = []
-        n_l = self.H_cycles * self.L_cycles
-        for i in range(self.H_cycles):
-            for k in range(i * self.L_cycles, (i + 1) * self.L_cycles):
-                plan.append(("L", k, k >= n_l - l_bp))
-            plan.append(("H", i, i >= self.H_cycles - h_bp))
-        return plan
+        return hierarchical_plan(self.H_cycles, self.L_cycles, h_bp, l_bp)
 
-    def forward(self, carry, x: Tensor, cache: Optional[dict] = None, bp_steps: int = 2, **seq_info):
-        z_H, z_L = x, self.zL_init
-        grad_on = torch.is_grad_enabled()
-        for level, idx, grad in self.call_plan(bp_steps):
-            with torch.set_grad_enabled(grad_on and grad):
-                if level == "L":
-                    z_L = self.L_level(z_L, z_H, cache=None if cache is None else cache["L"][idx], **seq_info)
-                else:
-                    z_H = self.H_level(z_H, z_L, cache=None if cache is None else cache["H"][idx], **seq_info)
-        return None, z_H
+    def initial_states(self, x: Tensor) -> dict[str, Tensor]:
+        return {"H": x, "L": self.zL_init}
 
     def compute_train_extra_args(self, train_state: Any) -> dict[str, Any]:
         return dict(bp_steps=bp_steps_schedule(train_state.step, train_state.total_steps, self.bp_warmup_ratio,
                                                self.bp_min_steps, self.bp_max_steps))
-
-    def initial_carry(self, batch_size: int, dtype: torch.dtype) -> None:
-        return None

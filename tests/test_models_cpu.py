@@ -41,8 +41,11 @@ def test_call_plan_matches_recurrence():
     cfg = arch_preset("hrm", "L") | dict(vocab_size=512, max_seq_len=64, n_layers=2, hidden_size=256, num_heads=2)
     m = build_model(cfg).model
     plan = m.call_plan(5)
-    assert [lvl for lvl, _, _ in plan] == ["L", "L", "L", "H", "L", "L", "L", "H"]
-    assert [g for _, _, g in plan] == [False, False, False, True, True, True, True, True]
+    assert [c.state for c in plan] == ["L", "L", "L", "H", "L", "L", "L", "H"]
+    assert [c.inject for c in plan] == ["H", "H", "H", "L", "H", "H", "H", "L"]
+    assert [c.grad for c in plan] == [False, False, False, True, True, True, True, True]
+    assert [c.slot for c in plan][:4] == [("L", 0), ("L", 1), ("L", 2), ("H", 0)]
+    assert [c.grad for c in m.call_plan(2)] == [False] * 6 + [True, True]
 
 
 def test_prefixlm_mask():
@@ -79,3 +82,29 @@ def test_every_family_trains_on_cpu(net):
     loss, metrics = eng.train_step(batch, lr=1e-3, **extra)
     assert torch.isfinite(loss)
     assert metrics["loss"][1] > 0
+
+
+def test_family_call_plans_and_cache_layouts():
+    base = dict(vocab_size=512, max_seq_len=64, n_layers=2, hidden_size=256, num_heads=2)
+    trm = build_model(arch_preset("trm_match_recurrence", "L") | base).model
+    plan = trm.call_plan()
+    assert {c.stack for c in plan} == {"L_level"}
+    assert [c.state for c in plan] == ["L", "L", "L", "H"] * 2
+    assert [c.grad for c in plan] == [False, False, False, True, True, True, True, True]
+
+    rins = build_model(arch_preset("rins", "L") | base).model
+    plan = rins.call_plan()
+    assert [c.stack for c in plan] == ["L_level"] * 7 + ["H_level"]
+    assert [c.grad for c in plan] == [False] * 3 + [True] * 5
+    assert plan[-1].inject is None and rins.output_state == "L"
+
+    ut = build_model(arch_preset("ut", "L") | base).model
+    assert [(c.slot, c.grad) for c in ut.call_plan()] == [((0,), False), ((1,), False), ((2,), True), ((3,), True)]
+
+    kw = dict(max_batch_size=1, max_seq_len=8, device="cpu", dtype=torch.float32)
+    hrm = build_model(arch_preset("hrm", "L") | base).model
+    cache = hrm.create_cache(**kw)
+    assert sorted(cache) == ["H", "L"] and len(cache["H"]) == 2 and len(cache["L"]) == 6
+    cache = rins.create_cache(**kw)
+    assert len(cache["L"]) == 7 and isinstance(cache["L"][0], list) and not isinstance(cache["H"][0], list)
+    assert isinstance(ut.create_cache(**kw), list) and len(ut.create_cache(**kw)) == 4
