@@ -23,6 +23,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "device_setup.h"
 
 namespace hrm {
 namespace attn {
@@ -105,10 +106,14 @@ __device__ __forceinline__ int bwd_cost(int len, int prefix, int k0) {
   return (len - qstart + 63) / 64;
 }
 
+// A packing whose last boundary lies past T, or whose tile lists would overflow `cap`, is
+// rejected as a whole: both lists are left empty and the total is set to 0 (so the tail
+// kernels zero every output row), and kErrBounds is reported to `err` (if non-null). Nothing
+// is then read or written outside the T rows.
 __global__ void __launch_bounds__(1024) schedule_kernel(const int* cu, const int* prefix_lens, int n_cu,
-                                                        int causal, int cap, int* sched) {
+                                                        int causal, int cap, int T, int* sched, int* err) {
   __shared__ int hist_f[kCostBuckets], hist_b[kCostBuckets];
-  __shared__ int first_bad;
+  __shared__ int first_bad, tot_f, tot_b, reject;
   int4* fwd_tiles = reinterpret_cast<int4*>(sched + SCHED_HEADER);
   int4* bwd_tiles = fwd_tiles + cap;
   for (int i = threadIdx.x; i < kCostBuckets; i += blockDim.x) hist_f[i] = hist_b[i] = 0;
@@ -134,7 +139,7 @@ __global__ void __launch_bounds__(1024) schedule_kernel(const int* cu, const int
       hist_f[b] = acc;
       acc += c;
     }
-    sched[0] = min(acc, cap);
+    tot_f = acc;
   } else if (threadIdx.x == 32) {
     int acc = 0;
     for (int b = kCostBuckets - 1; b >= 0; --b) {
@@ -142,24 +147,32 @@ __global__ void __launch_bounds__(1024) schedule_kernel(const int* cu, const int
       hist_b[b] = acc;
       acc += c;
     }
-    sched[1] = min(acc, cap);
-  } else if (threadIdx.x == 64) {
-    sched[2] = n_docs > 0 ? cu[n_docs] : 0;
-    sched[3] = n_docs;
-    sched[4] = sched[5] = sched[6] = sched[7] = 0;
+    tot_b = acc;
   }
   __syncthreads();
+  if (threadIdx.x == 0) {
+    const int total = n_docs > 0 ? cu[n_docs] : 0;
+    reject = (n_docs > 0 && (cu[0] < 0 || total > T)) || tot_f > cap || tot_b > cap;
+    sched[0] = reject ? 0 : tot_f;
+    sched[1] = reject ? 0 : tot_b;
+    sched[2] = reject ? 0 : total;
+    sched[3] = reject ? 0 : n_docs;
+    sched[4] = sched[5] = sched[6] = sched[7] = 0;
+    if (reject) report_error(err, kErrBounds, 50);
+  }
+  __syncthreads();
+  if (reject) return;
   for (int d = threadIdx.x; d < n_docs; d += blockDim.x) {
     const int start = cu[d];
     const int len = cu[d + 1] - start;
     const int p = causal ? 0 : min(prefix_lens[d], len);
     for (int q0 = 0; q0 < len; q0 += 128) {
       const int slot = atomicAdd(&hist_f[min(fwd_cost(len, p, q0), kCostBuckets - 1)], 1);
-      if (slot < cap) fwd_tiles[slot] = make_int4(start, len, p, q0);
+      fwd_tiles[slot] = make_int4(start, len, p, q0);
     }
     for (int k0 = 0; k0 < len; k0 += 128) {
       const int slot = atomicAdd(&hist_b[min(bwd_cost(len, p, k0), kCostBuckets - 1)], 1);
-      if (slot < cap) bwd_tiles[slot] = make_int4(start, len, p, k0);
+      bwd_tiles[slot] = make_int4(start, len, p, k0);
     }
   }
 }
@@ -739,23 +752,20 @@ at::Tensor device_error_word();
 
 int64_t attn_schedule_capacity(int64_t T, int64_t n_cu) { return (T + 127) / 128 + n_cu; }
 
-void attn_schedule(const at::Tensor& cu_seqlens, const at::Tensor& prefix_lens, bool causal, const at::Tensor& sched) {
+void attn_schedule(const at::Tensor& cu_seqlens, const at::Tensor& prefix_lens, bool causal, int64_t T,
+                   const at::Tensor& sched) {
   TORCH_CHECK(cu_seqlens.scalar_type() == at::kInt && prefix_lens.scalar_type() == at::kInt, "int32 metadata");
   c10::cuda::CUDAGuard guard(cu_seqlens.device());
   const int n_cu = (int)cu_seqlens.numel();
   const int64_t cap = (sched.numel() - attn::SCHED_HEADER) / 8;
   TORCH_CHECK(cap > 0, "schedule buffer too small");
   attn::schedule_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
-      cu_seqlens.data_ptr<int>(), prefix_lens.data_ptr<int>(), n_cu, causal ? 1 : 0, (int)cap, sched.data_ptr<int>());
+      cu_seqlens.data_ptr<int>(), prefix_lens.data_ptr<int>(), n_cu, causal ? 1 : 0, (int)cap, (int)T,
+      sched.data_ptr<int>(), device_error_word().data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-static int sm_count() {
-  int dev, n;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n;
-}
+static int sm_count() { return device_sm_count(); }
 
 void attn_fwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out, const at::Tensor& y,
               const at::Tensor& lse) {
@@ -775,11 +785,8 @@ void attn_fwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const a
   p.sched = sched.data_ptr<int>();
   p.cap = (int)((sched.numel() - attn::SCHED_HEADER) / 8);
   TORCH_CHECK(qkv.size(1) >= 4 * H * attn::D, "qkv width");
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::FWD_SMEM);
-    configured = true;
-  }
+  TORCH_CHECK(ensure_dynamic_smem((const void*)attn::attn_fwd_kernel, attn::FWD_SMEM) == cudaSuccess,
+              "cudaFuncSetAttribute failed");
   attn::attn_fwd_kernel<<<sm_count(), attn::FWD_THREADS, attn::FWD_SMEM, stream>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   attn::attn_zero_tail_kernel<<<64, 256, 0, stream>>>(p.out, p.y, p.ld_out, p.lse, p.T, p.H, p.sched);
@@ -823,11 +830,8 @@ void attn_bwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const a
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)attn::D));
   p.sched = sched.data_ptr<int>();
   p.cap = (int)((sched.numel() - attn::SCHED_HEADER) / 8);
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn::attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::BWD_SMEM);
-    configured = true;
-  }
+  TORCH_CHECK(ensure_dynamic_smem((const void*)attn::attn_bwd_kernel, attn::BWD_SMEM) == cudaSuccess,
+              "cudaFuncSetAttribute failed");
   attn::attn_bwd_kernel<<<sm_count(), attn::BWD_THREADS, attn::BWD_SMEM, stream>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   attn::attn_bwd_post_kernel<<<1024, 256, 0, stream>>>(p.dq_acc, p.dqkv, p.ld_dqkv, p.positions, p.cos_tab,
@@ -836,85 +840,3 @@ void attn_bwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const a
 }
 
 }  // namespace hrm
-
-// ---------------------------------------------------------------------------------------
-// Allocation-free attention forward (declared in attention_noalloc.h; no counterpart in
-// the reference). Same kernels as attn_fwd above; the schedule scratch is the static
-// device array below instead of a caller-provided tensor.
-// ---------------------------------------------------------------------------------------
-#include "attention_noalloc.h"
-
-namespace hrm {
-namespace attn {
-// Work schedule + counters for hrm_attn_fwd_noalloc, one per GPU that loads the library.
-static __device__ __align__(256) int g_noalloc_sched[HRM_ATTN_NOALLOC_SCRATCH_BYTES / 4];
-}  // namespace attn
-}  // namespace hrm
-
-namespace {
-constexpr int kMaxDevices = 64;
-int* g_noalloc_ptr[kMaxDevices] = {};
-int g_noalloc_sms[kMaxDevices] = {};
-
-// Once per device, with that device current: resolve the static array's device address
-// (host code must not use the symbol itself) and configure the kernel.
-cudaError_t noalloc_setup(int dev) {
-  if (g_noalloc_ptr[dev] != nullptr) return cudaSuccess;
-  void* ptr = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(&ptr, hrm::attn::g_noalloc_sched);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(hrm::attn::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           hrm::attn::FWD_SMEM);
-  if (e != cudaSuccess) return e;
-  int sms = 0;
-  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return e;
-  g_noalloc_sms[dev] = sms;
-  g_noalloc_ptr[dev] = static_cast<int*>(ptr);
-  return cudaSuccess;
-}
-}  // namespace
-
-extern "C" __attribute__((visibility("default"))) const char* hrm_attn_fwd_noalloc_strerror(int code) {
-  if (code == 0) return "success";
-  if (code == HRM_ATTN_NOALLOC_TOO_LARGE)
-    return "problem too large for the static scratch: need ceil(T/128) + n_cu <= HRM_ATTN_NOALLOC_MAX_TILES";
-  if (code == HRM_ATTN_NOALLOC_BAD_ARG) return "invalid argument (null pointer, head count or row stride)";
-  return cudaGetErrorString(static_cast<cudaError_t>(code));
-}
-
-extern "C" __attribute__((visibility("default"))) int hrm_attn_fwd_noalloc(
-    const void* qkv, long long ld_qkv, int T, int num_heads, const int* cu_seqlens, int n_cu, const int* prefix_lens,
-    int causal, void* out, void* y, long long ld_out, float* lse, cudaStream_t stream) {
-  if (qkv == nullptr || cu_seqlens == nullptr || prefix_lens == nullptr || out == nullptr || y == nullptr ||
-      lse == nullptr || T <= 0 || num_heads <= 0 || n_cu < 1 || ld_qkv < 4LL * num_heads * hrm::attn::D ||
-      ld_out < (long long)num_heads * hrm::attn::D || (ld_qkv % 8) != 0 || (ld_out % 8) != 0)
-    return HRM_ATTN_NOALLOC_BAD_ARG;
-  const long long tiles = (T + 127) / 128 + (long long)n_cu;
-  if (tiles > HRM_ATTN_NOALLOC_MAX_TILES) return HRM_ATTN_NOALLOC_TOO_LARGE;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return (int)e;
-  if (dev >= kMaxDevices) return HRM_ATTN_NOALLOC_BAD_ARG;
-  e = noalloc_setup(dev);
-  if (e != cudaSuccess) return (int)e;
-  int* sched = g_noalloc_ptr[dev];
-  const int cap = HRM_ATTN_NOALLOC_MAX_TILES;
-
-  hrm::attn::schedule_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, prefix_lens, n_cu, causal ? 1 : 0, cap, sched);
-  hrm::attn::FwdParams p{};
-  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
-  p.ld_qkv = ld_qkv;
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.y = static_cast<__nv_bfloat16*>(y);
-  p.ld_out = ld_out;
-  p.lse = lse;
-  p.T = T;
-  p.H = num_heads;
-  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hrm::attn::D));
-  p.sched = sched;
-  p.cap = cap;
-  hrm::attn::attn_fwd_kernel<<<g_noalloc_sms[dev], hrm::attn::FWD_THREADS, hrm::attn::FWD_SMEM, stream>>>(p);
-  hrm::attn::attn_zero_tail_kernel<<<64, 256, 0, stream>>>(p.out, p.y, p.ld_out, p.lse, p.T, p.H, p.sched);
-  return (int)cudaGetLastError();
-}

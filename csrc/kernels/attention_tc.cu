@@ -31,6 +31,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "device_setup.h"
 
 namespace hrm {
 namespace attn_tc {
@@ -1090,16 +1091,9 @@ void attn_fwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
   p.sched = sched.data_ptr<int>();
   p.err = device_error_word().data_ptr<int>();
 
-  static bool configured = false;
-  if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(attn_tc::attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     attn_tc::SMEM_BYTES) == cudaSuccess,
-                "cudaFuncSetAttribute failed");
-    configured = true;
-  }
-  int dev, sms;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  TORCH_CHECK(ensure_dynamic_smem((const void*)attn_tc::attn_fwd_tc_kernel, attn_tc::SMEM_BYTES) == cudaSuccess,
+              "cudaFuncSetAttribute failed");
+  const int sms = device_sm_count();
   attn_tc::attn_fwd_tc_kernel<<<sms, attn_tc::THREADS, attn_tc::SMEM_BYTES, stream>>>(map, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   attn_tc::zero_tail_kernel<<<64, 256, 0, stream>>>(p.out, p.y, p.ld_out, p.lse, T, (int)H, p.sched);
@@ -1197,16 +1191,9 @@ void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
   p.cap = (int)((sched.numel() - attn_tc::SCHED_HEADER) / 8);
   p.err = device_error_word().data_ptr<int>();
   p.profile = g_bwd_profile_enabled ? 1 : 0;
-  static bool configured = false;
-  if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(attn_tc::attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     attn_tc::BWD_SMEM_BYTES) == cudaSuccess,
-                "cudaFuncSetAttribute failed");
-    configured = true;
-  }
-  int dev, sms;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  TORCH_CHECK(ensure_dynamic_smem((const void*)attn_tc::attn_bwd_tc_kernel, attn_tc::BWD_SMEM_BYTES) == cudaSuccess,
+              "cudaFuncSetAttribute failed");
+  const int sms = device_sm_count();
   attn_tc::attn_bwd_tc_kernel<<<sms, attn_tc::BWD_THREADS, attn_tc::BWD_SMEM_BYTES, stream>>>(m_kv, m_q, m_do, m_dq,
                                                                                                p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -1216,3 +1203,168 @@ void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
 }
 
 }  // namespace hrm
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free attention forward (declared in attention_noalloc.h; no counterpart in the
+// reference). It runs the same tcgen05 forward as attn_fwd_tc above; the work schedule and
+// the error word live in the file-scope device array below instead of in memory that a
+// caller or torch allocates.
+// ---------------------------------------------------------------------------------------
+#include "attention_noalloc.h"
+
+namespace hrm {
+namespace attn {
+__global__ void schedule_kernel(const int* cu, const int* prefix_lens, int n_cu, int causal, int cap, int T,
+                                int* sched, int* err);
+}  // namespace attn
+namespace attn_tc {
+// Ints [0, kNoallocErrOffset): the schedule (header, forward and backward tile lists, 8 ints
+// per tile); then the 4-int error word. One copy per GPU that loads the library.
+static __device__ __align__(256) int g_noalloc_scratch[HRM_ATTN_NOALLOC_SCRATCH_BYTES / 4];
+constexpr int kNoallocErrOffset = SCHED_HEADER + 8 * HRM_ATTN_NOALLOC_MAX_TILES;
+static_assert(kNoallocErrOffset % 4 == 0 && kNoallocErrOffset + 4 <= HRM_ATTN_NOALLOC_SCRATCH_BYTES / 4,
+              "allocation-free scratch layout");
+}  // namespace attn_tc
+}  // namespace hrm
+
+namespace {
+struct NoallocDevice {
+  std::atomic<int*> scratch{nullptr};  // published last (release), after `sms`
+  int sms = 0;
+};
+NoallocDevice g_noalloc[hrm::kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: the static array's device address (host code
+// must not use the symbol itself as a pointer), the kernel's shared-memory limit and the SM
+// count. Host threads that race on the first call serialise on the mutex.
+cudaError_t noalloc_setup(int dev, int** scratch, int* sms) {
+  int* ptr = g_noalloc[dev].scratch.load(std::memory_order_acquire);
+  if (ptr == nullptr) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    ptr = g_noalloc[dev].scratch.load(std::memory_order_relaxed);
+    if (ptr == nullptr) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, hrm::attn_tc::g_noalloc_scratch);
+      if (e != cudaSuccess) return e;
+      e = hrm::ensure_dynamic_smem((const void*)hrm::attn_tc::attn_fwd_tc_kernel, hrm::attn_tc::SMEM_BYTES);
+      if (e != cudaSuccess) return e;
+      int n = 0;
+      e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return e;
+      g_noalloc[dev].sms = n;
+      ptr = static_cast<int*>(p);
+      g_noalloc[dev].scratch.store(ptr, std::memory_order_release);
+    }
+  }
+  *scratch = ptr;
+  *sms = g_noalloc[dev].sms;
+  return cudaSuccess;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, without exceptions.
+CUresult noalloc_encode(CUtensorMap* map, void* base, int width, int T, long long ld) {
+  using EncodeTiledFn = hrm::EncodeTiledFn;
+  static std::atomic<EncodeTiledFn> fn{nullptr};
+  EncodeTiledFn f = fn.load(std::memory_order_acquire);
+  if (f == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        ptr == nullptr)
+      return CUDA_ERROR_NOT_FOUND;
+    f = reinterpret_cast<EncodeTiledFn>(ptr);
+    fn.store(f, std::memory_order_release);
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)T};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return f(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <typename... P, typename... A>
+cudaError_t noalloc_launch(void (*kernel)(P...), int grid, int block, int smem, cudaStream_t stream, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) const char* hrm_attn_fwd_noalloc_strerror(int code) {
+  if (code == 0) return "success";
+  if (code == HRM_ATTN_NOALLOC_TOO_LARGE)
+    return "problem too large for the static scratch: need ceil(T/128) + n_cu <= HRM_ATTN_NOALLOC_MAX_TILES";
+  if (code == HRM_ATTN_NOALLOC_BAD_ARG)
+    return "invalid argument (null or misaligned pointer, head count, row stride or device index)";
+  if (code == HRM_ATTN_NOALLOC_TENSOR_MAP) return "cuTensorMapEncodeTiled rejected the qkv layout";
+  return cudaGetErrorString(static_cast<cudaError_t>(code));
+}
+
+extern "C" __attribute__((visibility("default"))) int hrm_attn_fwd_noalloc(
+    const void* qkv, long long ld_qkv, int T, int num_heads, const int* cu_seqlens, int n_cu, const int* prefix_lens,
+    int causal, void* out, void* y, long long ld_out, float* lse, cudaStream_t stream) {
+  const uintptr_t vec = reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(out) |
+                        reinterpret_cast<uintptr_t>(y);
+  const uintptr_t word = reinterpret_cast<uintptr_t>(lse) | reinterpret_cast<uintptr_t>(cu_seqlens) |
+                         reinterpret_cast<uintptr_t>(prefix_lens);
+  if (qkv == nullptr || cu_seqlens == nullptr || prefix_lens == nullptr || out == nullptr || y == nullptr ||
+      lse == nullptr || T <= 0 || num_heads <= 0 || n_cu < 1 ||
+      ld_qkv < 4LL * num_heads * hrm::attn_tc::D || ld_out < (long long)num_heads * hrm::attn_tc::D ||
+      (ld_qkv % 8) != 0 || (ld_out % 8) != 0 || (vec & 15) != 0 || (word & 3) != 0)
+    return HRM_ATTN_NOALLOC_BAD_ARG;
+  const long long tiles = (T + 127) / 128 + (long long)n_cu;
+  if (tiles > HRM_ATTN_NOALLOC_MAX_TILES) return HRM_ATTN_NOALLOC_TOO_LARGE;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= hrm::kMaxDevices) return HRM_ATTN_NOALLOC_BAD_ARG;
+  int* scratch = nullptr;
+  int sms = 0;
+  e = noalloc_setup(dev, &scratch, &sms);
+  if (e != cudaSuccess) return (int)e;
+
+  CUtensorMap map;
+  if (noalloc_encode(&map, const_cast<void*>(qkv), 4 * num_heads * hrm::attn_tc::D, T, ld_qkv) != CUDA_SUCCESS)
+    return HRM_ATTN_NOALLOC_TENSOR_MAP;
+
+  int* sched = scratch;
+  int* err = scratch + hrm::attn_tc::kNoallocErrOffset;
+  hrm::attn_tc::Params p{};
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.ld_out = (long)ld_out;
+  p.ld_qkv = (long)ld_qkv;
+  p.lse = lse;
+  p.T = T;
+  p.H = num_heads;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hrm::attn_tc::D));
+  p.sched = sched;
+  p.err = err;
+
+  // Each step returns its own launch status (no cudaGetLastError: that would also report,
+  // and clear, an error left by some other caller on this thread).
+  e = cudaMemsetAsync(err, 0, 4 * sizeof(int), stream);  // the error word starts at zero every call
+  if (e != cudaSuccess) return (int)e;
+  e = noalloc_launch(hrm::attn::schedule_kernel, 1, 1024, 0, stream, cu_seqlens, prefix_lens, n_cu,
+                     causal ? 1 : 0, (int)HRM_ATTN_NOALLOC_MAX_TILES, T, sched, err);
+  if (e != cudaSuccess) return (int)e;
+  e = noalloc_launch(hrm::attn_tc::attn_fwd_tc_kernel, sms, hrm::attn_tc::THREADS, hrm::attn_tc::SMEM_BYTES, stream,
+                     map, p);
+  if (e != cudaSuccess) return (int)e;
+  e = noalloc_launch(hrm::attn_tc::zero_tail_kernel, 64, 256, 0, stream, p.out, p.y, p.ld_out, p.lse, T, num_heads,
+                     (const int*)sched);
+  return (int)e;
+}
+
+extern "C" __attribute__((visibility("default"))) int hrm_attn_fwd_noalloc_status(int* code4) {
+  if (code4 == nullptr) return HRM_ATTN_NOALLOC_BAD_ARG;
+  const cudaError_t e = cudaMemcpyFromSymbol(code4, hrm::attn_tc::g_noalloc_scratch, 4 * sizeof(int),
+                                             hrm::attn_tc::kNoallocErrOffset * sizeof(int), cudaMemcpyDeviceToHost);
+  return (int)e;
+}

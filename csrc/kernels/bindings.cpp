@@ -21,7 +21,8 @@ void gemm_f2(const at::Tensor& dy, const at::Tensor& x, int64_t M, int64_t N, in
              int64_t shard_rows, int64_t inbox_stride, int64_t rank, int64_t world, const at::Tensor& hyper,
              double beta1, double beta2, double wd, double ema_decay, bool has_m, bool has_ema);
 int64_t attn_schedule_capacity(int64_t T, int64_t n_cu);
-void attn_schedule(const at::Tensor& cu_seqlens, const at::Tensor& prefix_lens, bool causal, const at::Tensor& sched);
+void attn_schedule(const at::Tensor& cu_seqlens, const at::Tensor& prefix_lens, bool causal, int64_t T,
+                   const at::Tensor& sched);
 void attn_fwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out, const at::Tensor& y,
               const at::Tensor& lse);
 void attn_fwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,

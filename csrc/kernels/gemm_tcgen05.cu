@@ -38,6 +38,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "device_setup.h"
 
 namespace hrm {
 
@@ -823,24 +824,18 @@ CUtensorMap make_map(const at::Tensor& t, int64_t inner, int64_t outer, int64_t 
   return map;
 }
 
-int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
-}
+int num_sms() { return device_sm_count(); }
 
 // CTA pairs that can be resident at once (cluster placement can leave SMs unused).
 template <int A_MN, int B_MN, int EPI>
 int max_pair_clusters() {
-  static int n = 0;
+  static std::atomic<int> per_device[kMaxDevices];  // per kernel instantiation and device
+  const int dev = current_device();
+  TORCH_CHECK(dev < kMaxDevices, "device index out of range");
+  int n = per_device[dev].load(std::memory_order_acquire);
   if (n == 0) {
     auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 0, 1>;
-    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem_bytes<EPI>()) ==
-                    cudaSuccess,
+    TORCH_CHECK(ensure_dynamic_smem((const void*)kern, pair_smem_bytes<EPI>()) == cudaSuccess,
                 "cudaFuncSetAttribute failed");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms() / 2));
@@ -857,6 +852,7 @@ int max_pair_clusters() {
     TORCH_CHECK(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters > 0,
                 "no CTA pair of the GEMM fits on this device");
     n = std::min(clusters, num_sms() / 2);
+    per_device[dev].store(n, std::memory_order_release);
   }
   return n;
 }
@@ -885,13 +881,8 @@ void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a
 template <int A_MN, int B_MN, int EPI, int F1 = 0>
 void launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int grid, cudaStream_t stream) {
   auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, F1>;
-  static bool configured = false;
-  if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes<EPI>()) ==
-                    cudaSuccess,
-                "cudaFuncSetAttribute failed");
-    configured = true;
-  }
+  TORCH_CHECK(ensure_dynamic_smem((const void*)kern, gemm_smem_bytes<EPI>()) == cudaSuccess,
+              "cudaFuncSetAttribute failed");
   kern<<<grid, GEMM_THREADS, gemm_smem_bytes<EPI>(), stream>>>(ma, mb, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

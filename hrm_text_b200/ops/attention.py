@@ -35,7 +35,7 @@ class PackedSeq:
         if sched is None:
             cap = cuda().attn_schedule_capacity(self.T, self.cu_seqlens.numel())
             sched = torch.empty(8 + 8 * cap, dtype=torch.int32, device=self.cu_seqlens.device)
-            cuda().attn_schedule(self.cu_seqlens, self.prefix_lens, causal, sched)
+            cuda().attn_schedule(self.cu_seqlens, self.prefix_lens, causal, self.T, sched)
             self._sched[causal] = sched
         return sched
 

@@ -32,9 +32,25 @@ def random_packing(T: int, seed: int = 0, max_doc: int = 700, causal_frac: bool 
     return torch.from_numpy(cu), torch.from_numpy(pl), torch.from_numpy(pos), total
 
 
-def assert_close(actual, expected, rel=2e-2, name=""):
+def assert_close(actual, expected, rel=2e-2, name="", atol=None):
+    """Element-wise ``|actual - expected| <= atol + rel * |expected|``.
+
+    ``atol`` defaults to ``rel`` times the RMS of ``expected`` (not its maximum), so a wrong
+    region of small values -- a masked tile, a padding head, a short document -- cannot hide
+    behind the largest entries of the tensor. Non-finite values always fail.
+    """
     actual = actual.float()
     expected = expected.float()
-    scale = expected.abs().max().item() + 1e-6
-    err = (actual - expected).abs().max().item()
-    assert err <= rel * scale, f"{name}: max abs err {err:.4g} vs scale {scale:.4g} (rel {err / scale:.3g})"
+    assert actual.shape == expected.shape, f"{name}: shape {tuple(actual.shape)} vs {tuple(expected.shape)}"
+    assert torch.isfinite(actual).all().item(), f"{name}: non-finite values"
+    if atol is None:
+        atol = rel * (expected.pow(2).mean().sqrt().item() + 1e-6)
+    diff = (actual - expected).abs()
+    excess = diff - (atol + rel * expected.abs())
+    worst = int(excess.flatten().argmax().item())
+    if excess.flatten()[worst].item() > 0:
+        idx = np.unravel_index(worst, tuple(actual.shape))
+        raise AssertionError(
+            f"{name}: element {tuple(int(i) for i in idx)} = {actual.flatten()[worst].item():.5g}, expected "
+            f"{expected.flatten()[worst].item():.5g} (|diff| {diff.flatten()[worst].item():.4g} > atol {atol:.4g} "
+            f"+ {rel:g}*|expected|); {(excess > 0).sum().item()} of {excess.numel()} elements out of tolerance")

@@ -8,12 +8,16 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("causal", [False, True])
-def test_attention_fwd_bwd(cuda_device, causal):
+@pytest.mark.parametrize("T,H,seed,max_doc", [(2048, 2, 1, 700), (640, 1, 4, 130), (3000, 3, 5, 1500)])
+def test_attention_fwd_bwd(cuda_device, causal, T, H, seed, max_doc):
+    """tcgen05 forward and backward against the fp32 oracle on ragged packings: documents of
+    length 1, 2, 64, 129 and 130, prefix 0 and prefix == length, T not a multiple of 128 and a
+    padded tail."""
     from hrm_text_b200.models.layers import prefixlm_attention_reference
     from hrm_text_b200.ops.attention import flash_attn_varlen_prefixlm
-    torch.manual_seed(0)
-    T, H, D = 2048, 2, 128
-    cu, pl, pos, total = random_packing(T, seed=1)
+    torch.manual_seed(seed)
+    D = 128
+    cu, pl, pos, total = random_packing(T, seed=seed, max_doc=max_doc)
     q, k, v = (torch.randn(T, H, D, device=cuda_device).bfloat16().requires_grad_(True) for _ in range(3))
     out = flash_attn_varlen_prefixlm(q, k, v, causal, pl.to(cuda_device), None, cu.to(cuda_device))
     qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
