@@ -28,6 +28,7 @@ from typing import Any, Callable, Optional
 import torch
 from torch import Tensor, nn
 
+from ...utils.trace import nvtx
 from ..common import trunc_normal_init_
 
 
@@ -92,7 +93,8 @@ def run_plan(model: nn.Module, plan: list[ModuleCall], states: dict[str, Tensor]
     grad_on = torch.is_grad_enabled()
     for call in plan:
         stack = getattr(model, call.stack)
-        with torch.set_grad_enabled(grad_on and call.grad):
+        with nvtx(f"{call.stack}{list(call.slot)}{' grad' if call.grad else ''}"), \
+                torch.set_grad_enabled(grad_on and call.grad):
             states[call.state] = stack(states[call.state], None if call.inject is None else states[call.inject],
                                        cache=lookup(cache, call.slot), **seq_info)
     return states

@@ -24,6 +24,7 @@ import torch
 from torch import Tensor
 
 from .._native import cuda
+from ..utils.trace import nvtx
 from . import gemm as G
 from .attention import PackedSeq, attention_bwd, attention_fwd, rope_half_tables
 
@@ -70,18 +71,25 @@ class FusedPreNormBlock(torch.autograd.Function):
                 causal: bool, train: bool):
         cos, sin = rope
         hidden = w_o.shape[0]
-        xn, r1, s = rmsnorm(x, eps, injection)
+        with nvtx("rmsnorm.fwd"):
+            xn, r1, s = rmsnorm(x, eps, injection)
         sched = packed.schedule(causal)
         f1_qkv, f1_gu = getattr(w_gqkv, "_f1", None), getattr(w_gu, "_f1", None)
-        if f1_qkv is None:
-            gqkv = G.linear_rope(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden)
-        else:
-            gqkv = G.linear_rope_f1(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden, f1_qkv)
-        o, y, lse = attention_fwd(gqkv, num_heads, sched)
-        x1 = G.linear(y, w_o, residual=s)
-        xn2, r2, _ = rmsnorm(x1, eps)
-        gu, h = G.linear_swiglu(xn2, w_gu) if f1_gu is None else G.linear_swiglu_f1(xn2, w_gu, f1_gu)
-        x2 = G.linear(h, w_d, residual=x1)
+        with nvtx("gemm.gqkv_rope"):
+            if f1_qkv is None:
+                gqkv = G.linear_rope(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden)
+            else:
+                gqkv = G.linear_rope_f1(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden, f1_qkv)
+        with nvtx("attention.fwd"):
+            o, y, lse = attention_fwd(gqkv, num_heads, sched)
+        with nvtx("gemm.o_residual"):
+            x1 = G.linear(y, w_o, residual=s)
+        with nvtx("rmsnorm.fwd"):
+            xn2, r2, _ = rmsnorm(x1, eps)
+        with nvtx("gemm.gate_up_swiglu"):
+            gu, h = G.linear_swiglu(xn2, w_gu) if f1_gu is None else G.linear_swiglu_f1(xn2, w_gu, f1_gu)
+        with nvtx("gemm.down_residual"):
+            x2 = G.linear(h, w_d, residual=x1)
         if train:
             for w in (w_gqkv, w_o, w_gu, w_d):
                 if getattr(w, "_f2", None) is not None:
@@ -100,19 +108,30 @@ class FusedPreNormBlock(torch.autograd.Function):
         dx2 = dx2.contiguous()
         grads = [None] * 4
         # MLP
-        dgu = G.linear_dgrad_swiglu(dx2, w_d, gu)
-        _wgrad(dx2, h, w_d, grads, 3)
-        dxn2 = G.linear_dgrad(dgu, w_gu)
-        _wgrad(dgu, xn2, w_gu, grads, 2)
-        dx1 = rmsnorm_bwd(dxn2, x1, r2, dres=dx2)
+        with nvtx("gemm.down_dgrad_swiglu"):
+            dgu = G.linear_dgrad_swiglu(dx2, w_d, gu)
+        with nvtx("gemm.wgrad"):
+            _wgrad(dx2, h, w_d, grads, 3)
+        with nvtx("gemm.dgrad"):
+            dxn2 = G.linear_dgrad(dgu, w_gu)
+        with nvtx("gemm.wgrad"):
+            _wgrad(dgu, xn2, w_gu, grads, 2)
+        with nvtx("rmsnorm.bwd"):
+            dx1 = rmsnorm_bwd(dxn2, x1, r2, dres=dx2)
         # attention
-        dy = G.linear_dgrad(dx1, w_o)
-        _wgrad(dx1, y, w_o, grads, 1)
-        dgqkv = attention_bwd(gqkv, ctx.num_heads, packed.schedule(ctx.causal), o, lse, dy, packed.position_ids,
-                              cos, sin)
-        dxn = G.linear_dgrad(dgqkv, w_gqkv)
-        _wgrad(dgqkv, xn, w_gqkv, grads, 0)
-        ds = rmsnorm_bwd(dxn, s, r1, dres=dx1)
+        with nvtx("gemm.dgrad"):
+            dy = G.linear_dgrad(dx1, w_o)
+        with nvtx("gemm.wgrad"):
+            _wgrad(dx1, y, w_o, grads, 1)
+        with nvtx("attention.bwd"):
+            dgqkv = attention_bwd(gqkv, ctx.num_heads, packed.schedule(ctx.causal), o, lse, dy,
+                                  packed.position_ids, cos, sin)
+        with nvtx("gemm.dgrad"):
+            dxn = G.linear_dgrad(dgqkv, w_gqkv)
+        with nvtx("gemm.wgrad"):
+            _wgrad(dgqkv, xn, w_gqkv, grads, 0)
+        with nvtx("rmsnorm.bwd"):
+            ds = rmsnorm_bwd(dxn, s, r1, dres=dx1)
         d_inj = ds if ctx.has_injection else None
         return (ds, d_inj, grads[0], grads[1], grads[2], grads[3], None, None, None, None, None, None)
 

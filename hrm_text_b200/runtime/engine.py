@@ -33,6 +33,7 @@ import torch.distributed as dist
 from torch import Tensor, nn
 
 from ..optim.adam_atan2 import reference_update
+from ..utils.trace import nvtx
 
 
 @dataclass
@@ -323,16 +324,21 @@ class TrainEngine:
 
     def forward_backward(self, batch: dict, **extra):
         self.params.zero_grad()
-        self.carry, loss, metrics = self.model(carry=self.carry, batch=batch, **extra)
-        loss.backward()
+        with nvtx("forward"):
+            self.carry, loss, metrics = self.model(carry=self.carry, batch=batch, **extra)
+        with nvtx("backward"):
+            loss.backward()
         self.params.collect_autograd_grads()
         return loss.detach(), metrics
 
     def step_body(self, batch: dict, **extra):
         loss, metrics = self.forward_backward(batch, **extra)
-        self.params.reduce_grads()
-        self.params.optimizer_step()
-        self.params.gather_params()
+        with nvtx("reduce_grads"):
+            self.params.reduce_grads()
+        with nvtx("optimizer"):
+            self.params.optimizer_step()
+        with nvtx("gather"):
+            self.params.gather_params()
         return loss, metrics
 
     def train_step(self, batch: dict, lr: float, **extra):

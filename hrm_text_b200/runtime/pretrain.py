@@ -31,6 +31,7 @@ from ..registry import get_model_source_path
 from ..utils.logging import MetricLogger
 from . import checkpoint as ckpt
 from .factory import build_model, model_config_dict
+from .perf import ThroughputMeter, step_flops
 from .trainer import Trainer
 from .watchdog import Heartbeat, StepWatchdog
 from ..utils.errors import check_device_errors
@@ -152,6 +153,7 @@ def run(config_name: str, overrides: list[str], max_steps: Optional[int] = None,
     if dist.is_initialized() and os.environ.get("HRM_HEARTBEAT", "0") == "1":
         heartbeat = Heartbeat(dist.distributed_c10d._get_default_store(), rank, world)
 
+    meter = ThroughputMeter(device, world)
     last, lr = {}, 0.0
     for epoch in range(1, config.epochs + 1):
         for batch, _info in loader:
@@ -160,7 +162,9 @@ def run(config_name: str, overrides: list[str], max_steps: Optional[int] = None,
             extra = model.compute_train_extra_args(state)
             if watchdog is not None:
                 watchdog.arm(state.step)
+            flops = step_flops(model, batch, extra)
             _loss, metrics = trainer.train_step_async(batch, lr, extra.get("bp_steps"))
+            meter.step(local_batch * world, flops)
             if heartbeat is not None:
                 heartbeat.set_step(state.step)
             if state.step % config.log_interval == 0:
@@ -171,8 +175,9 @@ def run(config_name: str, overrides: list[str], max_steps: Optional[int] = None,
                     if stale:
                         raise RuntimeError(f"ranks {stale} stopped heart-beating; aborting before the next collective")
                 reduced = reduce_metrics(metrics, "train/", rank)
+                perf = meter.report()
                 if rank == 0:
-                    last = reduced | extra | {"train/lr": lr}
+                    last = reduced | extra | {"train/lr": lr} | perf
                     logger.log(last, step=state.step)
             if max_steps is not None and state.step >= max_steps:
                 break
