@@ -216,6 +216,7 @@ def run_ours(args):
         e2e = {"value": global_batch * args.steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": h2d_bytes,
                "d2h_bytes_per_step": 4, "ms_per_step": 1000.0 * wall / args.steps}
 
+    peak_gb = torch.cuda.max_memory_allocated() / 1e9
     launches_per_step = None if args.no_count else count_own_kernels(
         lambda: trainer.train_step_async(host_batches[0], lr=lr, bp_steps=bp))
     fused = getattr(trainer.engine.params, "fused", None) is not None
@@ -237,7 +238,7 @@ def run_ours(args):
                            if fused else "NCCL reduce-scatter / all-gather"),
                        "l2": "inputs larger than L2 (per-step working set >> 126 MB)"},
             "clocks": clock_info, "e2e": e2e, "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
-            "impl": "ours", "final_loss": last_loss,
+            "impl": "ours", "final_loss": last_loss, "peak_memory_gb": round(peak_gb, 2),
         }
         print(json.dumps(line), flush=True)
     import torch.distributed as dist

@@ -10,8 +10,9 @@
 //   warp 0      TMA loads: Q tile once, K and V blocks of 128 keys through 2-stage rings
 //               (128B-swizzled [128 rows][64] boxes straight from the fused gqkv buffer)
 //   warp 1      UMMA issue (one lane): S_j = Q K_j^T into one of two TMEM S buffers, then
-//               O_a += P_{j-1}[:, 0:64] V_{j-1}[0:64] and O_b += P_{j-1}[:, 64:128] V_{j-1}[64:128],
-//               so S_j runs on the tensor cores while the softmax warps turn S_{j-1} into P_{j-1}
+//               O_a += P_{j-1}[:, 0:64] V_{j-1}[0:64] and O_b += P_{j-1}[:, 64:128] V_{j-1}[64:128]
+//               with P read straight from TMEM (A operand in tensor memory), so S_j runs on
+//               the tensor cores while the softmax warps turn S_{j-1} into P_{j-1}
 //   warps 2..5  softmax of key half 0 of every block, warps 6..9 of key half 1: one query row
 //   and 6..9    per thread (TMEM lane quarter = warp % 4), 64 scores read from TMEM once into
 //               registers. Each half keeps its own running max / sum and its own O
@@ -21,8 +22,18 @@
 //               its row max grows by more than 8 (log2 units) -- exact, since O and l share
 //               the stale max. Two softmax warps per scheduler hide the TMEM/MUFU latency that
 //               one warp per scheduler cannot.
-// TMEM: S0 [0,128), S1 [128,256), O_a [256,384), O_b [384,512) (the whole 512 columns).
-// Shared memory: Q 32 KB, K 2 x 32 KB, V 2 x 32 KB, P 32 KB, per-row (max, sum) exchange 2 KB.
+// P stays in TMEM: a softmax half writes its 64 probabilities of block j as bf16 pairs into
+// the first 32 columns of its own 64-column half of block j's S buffer (the columns it has
+// just read), and the PV UMMA reads them from there. P_j and P_{j-1} thus live in different
+// buffers, so the softmax of block j never waits for PV_{j-1} (only an O rescale does), and
+// S_{j+2} may overwrite buffer j&1 as soon as PV_j has been issued: UMMAs of one thread run in
+// issue order.
+// Tile turnaround: Q is double-buffered (the next tile's Q arrives while this tile computes),
+// the producer passes each work item's tile descriptor through the shared-memory ring (no
+// role re-reads the schedule from global memory), and the softmax warps fetch their rows'
+// gate values into registers when a tile starts, so the epilogue does no global loads.
+// TMEM: S0/P0 [0,128), S1/P1 [128,256), O_a [256,384), O_b [384,512) (the whole 512 columns).
+// Shared memory: Q 2 x 32 KB, K 2 x 32 KB, V 2 x 32 KB, per-row (max, sum) exchange 2 KB.
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error, drains its own
 // copies and UMMAs, frees TMEM and returns.
@@ -138,22 +149,62 @@ struct Params {
   int* err;
 };
 
+// The forward's ring also carries each item's tile descriptor (read once, by the producer).
+struct TileRing {
+  uint64_t full[kItemRing], empty[kItemRing];
+  int item[kItemRing];
+  int4 tile[kItemRing];
+};
+__device__ __forceinline__ void tring_init(TileRing* r, int consumers) {
+  for (int i = 0; i < kItemRing; ++i) {
+    mbar_init(&r->full[i], 1);
+    mbar_init(&r->empty[i], consumers);
+  }
+}
+__device__ __forceinline__ bool tring_push(TileRing* r, int k, int* counter, const int4* tiles, int H, int n_items,
+                                           int& item, int4& tile) {
+  const int s = k % kItemRing;
+  if (!mbar_wait(&r->empty[s], ((k / kItemRing) & 1) ^ 1)) return false;
+  item = atomicAdd(counter, 1);
+  tile = item < n_items ? tiles[item / H] : make_int4(0, 0, 0, 0);
+  *reinterpret_cast<volatile int*>(&r->item[s]) = item;
+  r->tile[s] = tile;  // published by the release arrive below (the asm clobbers memory)
+  mbar_arrive(&r->full[s]);
+  return true;
+}
+__device__ __forceinline__ int tring_pop_thread(TileRing* r, int k, int4& tile) {
+  const int s = k % kItemRing;
+  if (!mbar_wait(&r->full[s], (k / kItemRing) & 1)) return INT_MAX;
+  const int it = *reinterpret_cast<volatile int*>(&r->item[s]);
+  tile = r->tile[s];
+  mbar_arrive(&r->empty[s]);
+  return it;
+}
+__device__ __forceinline__ int tring_pop_warp(TileRing* r, int k, int4& tile) {
+  const int s = k % kItemRing;
+  if (!__all_sync(0xffffffffu, mbar_wait(&r->full[s], (k / kItemRing) & 1))) return INT_MAX;
+  const int it = *reinterpret_cast<volatile int*>(&r->item[s]);
+  tile = r->tile[s];
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&r->empty[s]);
+  return it;
+}
+
 struct Barriers {
-  uint64_t q_full, q_empty;
+  uint64_t q_full[2], q_empty[2];
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_free[2];
+  uint64_t s_full[2];
   uint64_t p_full[2], o_done[2], o_free, ml_full, drain;
-  ItemRing ring;
+  TileRing ring;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + TILE_BYTES;          // 2 stages
-  uint8_t* sV = smem + 3 * TILE_BYTES;      // 2 stages
-  uint8_t* sP = smem + 5 * TILE_BYTES;
+  uint8_t* sQ = smem;                       // 2 stages
+  uint8_t* sK = smem + 2 * TILE_BYTES;      // 2 stages
+  uint8_t* sV = smem + 4 * TILE_BYTES;      // 2 stages
   float2* sML = reinterpret_cast<float2*>(smem + 6 * TILE_BYTES);
   Barriers* bar = reinterpret_cast<Barriers*>(smem + 6 * TILE_BYTES + ML_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
@@ -164,22 +215,21 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int4* tiles = reinterpret_cast<const int4*>(p.sched + SCHED_HEADER);
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar->q_full, 1);
-    mbar_init(&bar->q_empty, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->q_full[s], 1);
+      mbar_init(&bar->q_empty[s], 1);
       mbar_init(&bar->k_full[s], 1);
       mbar_init(&bar->k_empty[s], 1);
       mbar_init(&bar->v_full[s], 1);
       mbar_init(&bar->v_empty[s], 1);
       mbar_init(&bar->s_full[s], 1);
-      mbar_init(&bar->s_free[s], 256);
       mbar_init(&bar->p_full[s], 128);
       mbar_init(&bar->o_done[s], 1);
     }
     mbar_init(&bar->o_free, 256);
     mbar_init(&bar->ml_full, 256);
     mbar_init(&bar->drain, 1);
-    ring_init(&bar->ring, 9);  // UMMA thread + 8 softmax warps
+    tring_init(&bar->ring, 9);  // UMMA thread + 8 softmax warps
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
   }
@@ -203,20 +253,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------------------------- TMA loads
     if (lane == 0) {
       int n = 0, kv = 0;
-      int last_q = -1, last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
+      int last_q[2] = {-1, -1}, last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
       bool ok = true;
       for (int kk = 0; ok; ++kk, ++n) {
         int item;
-        if (!ring_push(&bar->ring, kk, const_cast<int*>(p.sched) + 4, item)) { report_error(p.err, kErrAttnWaitTimeout, 10); ok = false; break; }
+        int4 t;
+        if (!tring_push(&bar->ring, kk, const_cast<int*>(p.sched) + 4, tiles, p.H, n_items, item, t)) { report_error(p.err, kErrAttnWaitTimeout, 10); ok = false; break; }
         if (item >= n_items) break;
-        const int4 t = tiles[item / p.H];
         const int head = item % p.H;
         const int qx = (p.H + head) * D, kx = (2 * p.H + head) * D, vx = (3 * p.H + head) * D;
-        if (!mbar_wait(&bar->q_empty, (n & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 11); ok = false; break; }
-        mbar_arrive_expect_tx(&bar->q_full, TILE_BYTES);
-        tma_load_2d(sQ, &tm_qkv, &bar->q_full, qx, t.x + t.w);
-        tma_load_2d(sQ + TILE_BYTES / 2, &tm_qkv, &bar->q_full, qx + 64, t.x + t.w);
-        last_q = n;
+        const int qs = n & 1;
+        if (!mbar_wait(&bar->q_empty[qs], ((n >> 1) & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 11); ok = false; break; }
+        mbar_arrive_expect_tx(&bar->q_full[qs], TILE_BYTES);
+        tma_load_2d(sQ + qs * TILE_BYTES, &tm_qkv, &bar->q_full[qs], qx, t.x + t.w);
+        tma_load_2d(sQ + qs * TILE_BYTES + TILE_BYTES / 2, &tm_qkv, &bar->q_full[qs], qx + 64, t.x + t.w);
+        last_q[qs] = n >> 1;
         const int nb = tile_blocks(t);
         for (int j = 0; j < nb; ++j, ++kv) {
           const int s = kv & 1, r = kv >> 1;
@@ -234,8 +285,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (!ok) {  // drain this thread's copies in flight
-        if (last_q >= 0) mbar_wait(&bar->q_full, last_q & 1);
         for (int s = 0; s < 2; ++s) {
+          if (last_q[s] >= 0) mbar_wait(&bar->q_full[s], last_q[s] & 1);
           if (last_k[s] >= 0) mbar_wait(&bar->k_full[s], last_k[s] & 1);
           if (last_v[s] >= 0) mbar_wait(&bar->v_full[s], last_v[s] & 1);
         }
@@ -246,7 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, 0, 0);   // Q K^T: both K-major over d
       constexpr uint32_t idesc_pv = umma_idesc_bf16(128, 128, 0, 1);  // P V: P K-major over keys, V MN-major
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sP);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
       int n = 0, kv = 0;
       bool ok = true;
       auto wait_or_fail = [&](uint64_t* b, uint32_t par, int site) {
@@ -256,8 +307,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         return false;
       };
       // O_a += P[:, 0:64] V[0:64] and O_b += P[:, 64:128] V[64:128] for block `blk` (global
-      // block counter) of stage s, each as soon as its softmax half has written P; the first
-      // block of an item overwrites both accumulators
+      // block counter) of stage s, each as soon as its softmax half has written P into TMEM
+      // (half g: bf16 pairs in columns [g*64, g*64 + 32) of the block's S buffer, 8 columns
+      // per 16 keys); the first block of an item overwrites both accumulators
       auto issue_pv = [&](int blk, bool first) -> bool {
         const int s = blk & 1, r = blk >> 1;
         if (!wait_or_fail(&bar->v_full[s], r & 1, 22)) return false;
@@ -265,11 +317,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int g = 0; g < 2; ++g) {
           if (!wait_or_fail(&bar->p_full[g], blk & 1, 21)) return false;
           tc_fence_after();
+          const uint32_t p_tmem = tmem + (s ? TM_S1 : TM_S0) + g * 64;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 16 keys per step
-            const uint64_t a = umma_desc_sw128(p_base + g * (TILE_BYTES / 2) + k * 32, 16, 1024);
             const uint64_t b = umma_desc_sw128(v_base + s * TILE_BYTES + (g * 4 + k) * 2048, TILE_BYTES / 2, 1024);
-            umma_f16_ss(tmem + (g ? TM_OB : TM_OA), a, b, idesc_pv, (first && k == 0) ? 0u : 1u);
+            umma_f16_ts(tmem + (g ? TM_OB : TM_OA), p_tmem + k * 8, b, idesc_pv, (first && k == 0) ? 0u : 1u);
           }
           if (g == 1) umma_commit(&bar->v_empty[s]);
           umma_commit(&bar->o_done[g]);
@@ -277,28 +329,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       for (int kk = 0; ok; ++kk, ++n) {
-        const int item = ring_pop_thread(&bar->ring, kk);
+        int4 t;
+        const int item = tring_pop_thread(&bar->ring, kk, t);
         if (item == INT_MAX) { report_error(p.err, kErrAttnWaitTimeout, 9); ok = false; break; }
         if (item >= n_items) break;
-        const int4 t = tiles[item / p.H];
         const int nb = tile_blocks(t);
-        if (!wait_or_fail(&bar->q_full, n & 1, 23)) break;
+        const int qs = n & 1;
+        if (!wait_or_fail(&bar->q_full[qs], (n >> 1) & 1, 23)) break;
+        const uint32_t q_tile = q_base + qs * TILE_BYTES;
         const int first_blk = kv;
         for (int j = 0; j < nb && ok; ++j, ++kv) {
           const int s = kv & 1, r = kv >> 1;
           if (!wait_or_fail(&bar->k_full[s], r & 1, 24)) break;
-          if (!wait_or_fail(&bar->s_free[s], (r & 1) ^ 1, 25)) break;
+          // buffer s held S/P of block kv-2, whose PV was issued above in program order
           tc_fence_after();
           const uint32_t d_s = tmem + (s ? TM_S1 : TM_S0);
 #pragma unroll
           for (int k = 0; k < 8; ++k) {  // 16 dims per step
             const uint32_t off = (k >> 2) * (TILE_BYTES / 2) + (k & 3) * 32;
-            umma_f16_ss(d_s, umma_desc_sw128(q_base + off, 16, 1024),
+            umma_f16_ss(d_s, umma_desc_sw128(q_tile + off, 16, 1024),
                         umma_desc_sw128(k_base + s * TILE_BYTES + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
           }
           umma_commit(&bar->k_empty[s]);
           umma_commit(&bar->s_full[s]);
-          if (j == nb - 1) umma_commit(&bar->q_empty);
+          if (j == nb - 1) umma_commit(&bar->q_empty[qs]);
           if (j > 0) {
             if (j == 1 && !wait_or_fail(&bar->o_free, (n & 1) ^ 1, 26)) break;
             if (!issue_pv(kv - 1, j == 1)) break;
@@ -323,16 +377,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     int n = 0, kv = 0;
     bool ok = true;
     for (int kk = 0; ok; ++kk, ++n) {
-      const int item = ring_pop_warp(&bar->ring, kk);
+      int4 t;
+      const int item = tring_pop_warp(&bar->ring, kk, t);
       if (item == INT_MAX) { report_error(p.err, kErrAttnWaitTimeout, 8); ok = false; break; }
       if (item >= n_items) break;
-      const int4 t = tiles[item / p.H];
       const int head = item % p.H;
       const int doc_start = t.x, len = t.y, prefix = t.z, q0 = t.w;
       const int nb = tile_blocks(t);
       const int qi = q0 + row;                         // doc-relative query of this thread
       const int limit = min(len, max(prefix, qi + 1));  // keys [0, limit) are visible
       const int full_until = min(len, max(prefix, q0 + 1));
+      const bool row_ok = qi < len;
+      const long tok = (long)doc_start + qi;
+      // this row's 64 gate values of this half, fetched now and used by the epilogue
+      uint4 gate[8];
+      {
+        const uint4* grow = reinterpret_cast<const uint4*>(p.qkv + (row_ok ? tok : 0) * p.ld_qkv + head * D + wg * 64);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) gate[q] = row_ok ? __ldg(grow + q) : make_uint4(0, 0, 0, 0);
+      }
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < nb; ++j, ++kv) {
         const int s = kv & 1;
@@ -351,8 +414,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             v[e + 32] = __uint_as_float(r1[e]);
           }
         }
-        tc_fence_before();
-        mbar_arrive(&bar->s_free[s]);  // S is in registers: the next QK^T may overwrite it
         const int kbase = j * BKV + wg * 64;
         if (kbase + 64 > full_until) {  // partially visible half-block (uniform per warpgroup)
 #pragma unroll
@@ -366,51 +427,50 @@ __global__ void __launch_bounds__(THREADS, 1)
           mx1 = fmaxf(mx1, v[e + 1]);
         }
         const float bmax = fmaxf(mx0, mx1) * sl;  // scale > 0 commutes with max
-        // P_j overwrites this half of P_{j-1}: wait for its PV (also guards the O rescale)
-        if (!warp_wait(&bar->o_done[wg], (kv - 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 32); ok = false; break; }
-        tc_fence_after();
         // The rescale decision is per row, but tcgen05.ld/st are warp-collective
         // (.sync.aligned): decide per warp, and let rows that need no rescale use alpha = 1.
         const bool need = bmax > m_used + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? fast_exp2(m_used - bmax) : 1.f;  // 0 on the first block
-          if (j > 0) {
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              uint32_t r[32];
-              tmem_ld_32x32b_x32(tm_o + c * 32, r);
-              tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-              tmem_st_32x32b_x32(tm_o + c * 32, r);
-            }
-            tmem_st_wait();
-          }
+        const bool rescale = __any_sync(0xffffffffu, need);
+        float alpha = 1.f;
+        if (rescale) {
+          alpha = need ? fast_exp2(m_used - bmax) : 1.f;  // 0 on the first block
           if (need) {
             l *= alpha;
             m_used = bmax;
           }
         }
-        // P = exp2(s * scale - m_used) -> bf16 K-major swizzled box (row = query, 64 keys = 128 B)
+        // P = exp2(s * scale - m_used) as bf16 pairs, written over this half's S columns
         const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
-        uint8_t* prow = sP + wg * (TILE_BYTES / 2) + row * 128;
         float l0 = 0.f, l1 = 0.f;
+        {
+          uint32_t pk[32];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint32_t pk[4];
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const int e = q * 8 + 2 * w;
-            const float p0 = fast_exp2(fmaf(v[e], sl, neg_m));
-            const float p1 = fast_exp2(fmaf(v[e + 1], sl, neg_m));
+          for (int w = 0; w < 32; ++w) {
+            const float p0 = fast_exp2(fmaf(v[2 * w], sl, neg_m));
+            const float p1 = fast_exp2(fmaf(v[2 * w + 1], sl, neg_m));
             l0 += p0;
             l1 += p1;
             pk[w] = pack_bf16x2(p0, p1);
           }
-          *reinterpret_cast<uint4*>(prow + ((q ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          tmem_st_32x32b_x32(tmem + lane_off + (s ? TM_S1 : TM_S0) + wg * 64, pk);
         }
         l += l0 + l1;
-        fence_async_smem();
+        // O of this half may be rescaled only once PV_{kv-1} has landed; waiting every block
+        // (PV_{kv-1} is long done in the steady state) keeps the barrier's phase in step
+        if (!warp_wait(&bar->o_done[wg], (kv - 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 32); ok = false; break; }
+        tc_fence_after();
+        if (rescale && j > 0) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tm_o + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tmem_st_32x32b_x32(tm_o + c * 32, r);
+          }
+        }
+        tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bar->p_full[wg]);
       }
@@ -429,9 +489,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float l_all = l * sc_me + oth.y * sc_oth;
       const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
       const float sa = (wg == 0 ? sc_me : sc_oth) * inv, sb = (wg == 0 ? sc_oth : sc_me) * inv;
-      const bool row_ok = qi < len;
-      const long tok = (long)doc_start + qi;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int col = wg * 64 + c * 32;
         float va[32], vb[32];
@@ -449,11 +507,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (row_ok) {
           __nv_bfloat16* orow = p.out + tok * p.ld_out + head * D + col;
           __nv_bfloat16* yrow = p.y + tok * p.ld_out + head * D + col;
-          const uint4* grow = reinterpret_cast<const uint4*>(p.qkv + tok * p.ld_qkv + head * D + col);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const uint4 gv = grow[q];
-            const uint32_t* ga = &gv.x;
+            const uint4 gv = gate[c * 4 + q];
+            const uint32_t ga[4] = {gv.x, gv.y, gv.z, gv.w};
             uint32_t ow[4], yw[4];
 #pragma unroll
             for (int w = 0; w < 4; ++w) {

@@ -51,6 +51,7 @@ enum GemmEpilogue : int {
   EPI_SWIGLU_BWD = 5,
   EPI_CE = 6,
   EPI_F2 = 7,  // fp32 wgrad tile -> owner's inbox over NVLink; owner sums the slots and runs AdamATan2
+  EPI_CE_BWD = 8,  // recomputed logits -> (softmax - onehot) * dloss, bf16 (one V chunk of the LM head)
 };
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
@@ -716,6 +717,29 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           __syncwarp();
           if (lane == 0) atomicAdd_system(cnt, 1);
         }
+      } else if constexpr (EPI == EPI_CE_BWD) {
+        // Logits of one V chunk (columns [col0, col0 + N) of the head), recomputed by this GEMM
+        // and rounded to bf16 exactly as the forward's statistics saw them, turned into
+        // (softmax - onehot) * dloss with the forward's log-sum-exp; rows without a label are 0.
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+        const int label = row_ok ? args.labels[m] : -1;
+        const float lse = row_ok ? args.ce_max[m] : 0.f;  // natural-log LSE per row
+        const float g = *args.ce_sum;                     // d loss_sum
+        const int col0 = args.pair_offset;
+#pragma unroll 1
+        for (int c = half * 4; c < half * 4 + 4; ++c) {
+          float v[32];
+          tmem_load_f32x32(taddr + c * 32, v);
+          const int n = nt * BN + c * 32;
+          if (row_ok && n < args.N) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float prob = __expf(bf16_round(v[j]) - lse);
+              v[j] = label < 0 ? 0.f : (prob - (col0 + n + j == label ? 1.f : 0.f)) * g;
+            }
+            store_bf16x32(out + (long)m * args.ldo + n, v);
+          }
+        }
       } else if constexpr (EPI == EPI_CE) {
         // Partial softmax statistics over this warp's 128 columns; partial index nt*2 + half.
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
@@ -747,7 +771,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             run_sum = run_sum * fast_exp2((run_max - new_max) * kLog2e) + s;
             if (cmax > run_max) run_arg = n + carg;
             run_max = new_max;
-            store_bf16x32(out + (long)m * args.ldo + n, v);
+            if (out != nullptr) store_bf16x32(out + (long)m * args.ldo + n, v);  // null: statistics only
           }
         }
         if (row_ok) {
@@ -911,9 +935,14 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
-  args.out = out.data_ptr();
-  args.ldo = out.stride(0);
-  TORCH_CHECK(out.stride(1) == 1 && out.stride(0) % 8 == 0, "gemm: output rows must be contiguous and 16B aligned");
+  if (epi == EPI_CE && out.numel() == 0) {  // cross-entropy statistics without storing the logits
+    args.out = nullptr;
+    args.ldo = 0;
+  } else {
+    args.out = out.data_ptr();
+    args.ldo = out.stride(0);
+    TORCH_CHECK(out.stride(1) == 1 && out.stride(0) % 8 == 0, "gemm: output rows must be contiguous and 16B aligned");
+  }
   if (out2) { args.out2 = out2->data_ptr(); args.ldo2 = out2->stride(0); }
   if (residual) { args.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()); args.ldr = residual->stride(0); }
   if (aux) { args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr()); args.ldaux = aux->stride(0); }
@@ -968,6 +997,8 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
     HRM_GEMM_PAIR_CASE(0, 0, EPI_SWIGLU)
     HRM_GEMM_PAIR_CASE(0, 0, EPI_CE)
     HRM_GEMM_PAIR_CASE(0, 0, EPI_F32ADD)
+    HRM_GEMM_PAIR_CASE(0, 0, EPI_CE_BWD)
+    HRM_GEMM_PAIR_CASE(0, 1, EPI_F32ADD)
     HRM_GEMM_PAIR_CASE(0, 1, EPI_STORE)
     HRM_GEMM_PAIR_CASE(0, 1, EPI_RESIDUAL)
     HRM_GEMM_PAIR_CASE(0, 1, EPI_SWIGLU_BWD)
@@ -988,6 +1019,8 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   HRM_GEMM_CASE(0, 0, EPI_SWIGLU)
   HRM_GEMM_CASE(0, 0, EPI_CE)
   HRM_GEMM_CASE(0, 0, EPI_F32ADD)
+  HRM_GEMM_CASE(0, 0, EPI_CE_BWD)
+  HRM_GEMM_CASE(0, 1, EPI_F32ADD)
   HRM_GEMM_CASE(0, 1, EPI_STORE)
   HRM_GEMM_CASE(0, 1, EPI_RESIDUAL)
   HRM_GEMM_CASE(0, 1, EPI_SWIGLU_BWD)

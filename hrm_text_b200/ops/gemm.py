@@ -17,7 +17,7 @@ from torch import Tensor
 
 from .._native import cuda
 
-EPI_STORE, EPI_RESIDUAL, EPI_F32ADD, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_CE = range(7)
+EPI_STORE, EPI_RESIDUAL, EPI_F32ADD, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_CE, EPI_F2, EPI_CE_BWD = range(9)
 
 
 def _check(*tensors: Tensor) -> None:
@@ -96,20 +96,43 @@ def linear_wgrad_(dy: Tensor, x: Tensor, grad: Tensor) -> Tensor:
     return grad
 
 
-def lm_head_ce_logits(x: Tensor, w: Tensor, labels: Tensor):
-    """Logits ``x @ w.T`` (bf16) plus per-128-column partial softmax statistics."""
+def linear_dgrad_accumulate_(dy: Tensor, w: Tensor, acc: Tensor) -> Tensor:
+    """``acc += dy @ w`` in fp32 (``acc`` is ``[M, K]`` fp32, contiguous)."""
+    _check(dy, w)
+    assert acc.dtype == torch.float32 and acc.is_contiguous()
+    M, N = dy.shape
+    K = w.shape[1]
+    _gemm(dy, False, w, True, M, K, N, EPI_F32ADD, acc)
+    return acc
+
+
+def lm_head_ce_stats(x: Tensor, w: Tensor, labels: Tensor):
+    """Per-128-column softmax statistics of the logits ``x @ w.T`` (which are not stored):
+    ``(row max, sum of exp, argmax)`` per slice ``[2 * n_tiles, M]`` and the label logit ``[M]``."""
     _check(x, w)
     M, K = x.shape
     V = w.shape[0]
     n_tiles = 2 * ((V + 255) // 256)
-    logits = torch.empty((M, V), dtype=torch.bfloat16, device=x.device)
     pmax = torch.empty((n_tiles, M), dtype=torch.float32, device=x.device)
     psum = torch.empty((n_tiles, M), dtype=torch.float32, device=x.device)
     parg = torch.empty((n_tiles, M), dtype=torch.int32, device=x.device)
     tgt = torch.zeros((M,), dtype=torch.float32, device=x.device)
-    _gemm(x, False, w, False, M, V, K, EPI_CE, logits, labels=labels, ce_max=pmax, ce_sum=psum, ce_arg=parg,
+    no_logits = torch.empty((0,), dtype=torch.bfloat16, device=x.device)
+    _gemm(x, False, w, False, M, V, K, EPI_CE, no_logits, labels=labels, ce_max=pmax, ce_sum=psum, ce_arg=parg,
           ce_tgt=tgt)
-    return logits, pmax, psum, parg, tgt
+    return pmax, psum, parg, tgt
+
+
+def lm_head_ce_dlogits(x: Tensor, w_chunk: Tensor, labels: Tensor, lse: Tensor, grad: Tensor, col0: int,
+                       out: Tensor) -> Tensor:
+    """``out = (softmax - onehot(labels)) * grad`` for head rows ``[col0, col0 + w_chunk.shape[0])``,
+    with the logits recomputed as ``x @ w_chunk.T`` and normalised by the forward's ``lse``."""
+    _check(x, w_chunk)
+    M, K = x.shape
+    N = w_chunk.shape[0]
+    _gemm(x, False, w_chunk, False, M, N, K, EPI_CE_BWD, out, labels=labels, ce_max=lse, ce_sum=grad,
+          pair_offset=col0)
+    return out
 
 
 # ---------------------------------------------------------------------------------------

@@ -28,7 +28,9 @@ def test_attention_fwd_bwd(cuda_device, causal, T, H, seed, max_doc):
     out.backward(dout)
     ref.backward(dout.float())
     for a, b, name in ((q.grad, qr.grad, "dq"), (k.grad, kr.grad, "dk"), (v.grad, vr.grad, "dv")):
-        assert_close(a, b, 3e-2, name)
+        # bf16 P and dS (relative rounding 2^-8 each) summed over up to ~1500 keys: isolated
+        # elements land a few percent of the gradient's RMS away from the fp32 oracle
+        assert_close(a, b, 3e-2, name, atol=0.08 * b.float().pow(2).mean().sqrt().item())
         assert a[total:].abs().max().item() == 0.0
 
 

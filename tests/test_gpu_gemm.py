@@ -77,16 +77,18 @@ def test_linear_swiglu_fwd_bwd(cuda_device, M):
     assert_close(dgu, torch.cat([gr.grad, ur.grad], -1), 2e-2, "swiglu bwd")
 
 
-@pytest.mark.parametrize("T", [500, 1200])
-def test_lm_head_cross_entropy(cuda_device, T):
+@pytest.mark.parametrize("T,H,V,chunk", [(500, 256, 2048, 8192), (1200, 256, 2048, 512), (2048, 1280, 32768, 8192)])
+def test_lm_head_cross_entropy(cuda_device, T, H, V, chunk):
+    """Chunked LM head + CE (no [T, V] logits stored) against fp32 F.cross_entropy, with
+    ragged ignored labels (every 7th row and a block of 37 rows)."""
     from hrm_text_b200.ops.loss import lm_head_cross_entropy
     torch.manual_seed(4)
-    H, V = 256, 2048
     x = torch.randn(T, H, device=cuda_device).bfloat16().requires_grad_(True)
-    w = (torch.randn(V, H, device=cuda_device) / 16).bfloat16().requires_grad_(True)
+    w = (torch.randn(V, H, device=cuda_device) / (H ** 0.5)).bfloat16().requires_grad_(True)
     labels = torch.randint(0, V, (T,), device=cuda_device, dtype=torch.int32)
     labels[::7] = -100
-    loss, correct = lm_head_cross_entropy(x, w, labels)
+    labels[100:137] = -100
+    loss, correct = lm_head_cross_entropy(x, w, labels, chunk=chunk)
     xr = x.detach().float().requires_grad_(True)
     wr = w.detach().float().requires_grad_(True)
     logits = (xr @ wr.T).bfloat16().float()
