@@ -31,6 +31,8 @@ at::Tensor wait_flag_probe(const at::Tensor& flag, int64_t expected, double time
 at::Tensor sample_tokens(const at::Tensor& logits, double temp, int64_t seed, int64_t offset);
 at::Tensor decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                             const at::Tensor& total);
+at::Tensor decode_attention_gqkv(const at::Tensor& gqkv, int64_t H, const at::Tensor& k_cache,
+                                 const at::Tensor& v_cache, const at::Tensor& lengths);
 void attn_bwd_set_profile(bool enabled);
 at::Tensor attn_bwd_phase_counters(bool reset);
 void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
@@ -71,6 +73,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &hrm::attn_bwd);
   m.def("attn_bwd_tc", &hrm::attn_bwd_tc, "tcgen05 PrefixLM attention backward");
   m.def("decode_attention", &hrm::decode_attention, "split-KV decode attention against a static KV cache");
+  m.def("decode_attention_gqkv", &hrm::decode_attention_gqkv,
+        "decode step attention from the fused projection: KV append, split-KV attention, sigmoid gate");
   m.def("sample_tokens", &hrm::sample_tokens, "greedy / Gumbel-max token sampling (fused, one CTA per row)");
   m.def("wait_flag_probe", &hrm::wait_flag_probe, "bounded device wait on a flag (failure-detection probe)");
   m.def("attn_bwd_set_profile", &hrm::attn_bwd_set_profile, "enable per-phase clock tracing of attn_bwd_tc");

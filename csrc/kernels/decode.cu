@@ -16,6 +16,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "device_setup.h"
 
 namespace hrm {
 namespace {
@@ -32,14 +33,15 @@ __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
 __global__ void __launch_bounds__(WARPS * 32)
     decode_split_kernel(const __nv_bfloat16* __restrict__ q, long q_sb, long q_sh, const __nv_bfloat16* __restrict__ kc,
                         const __nv_bfloat16* __restrict__ vc, long c_sb, long c_ss, long c_sh,
-                        const int* __restrict__ total, int H, int chunk, float scale_log2,
+                        const int* __restrict__ total, int total_offset, int H, int chunk, float scale_log2,
+                        const __nv_bfloat16* __restrict__ gate, long g_sb, long g_sh,
                         __nv_bfloat16* __restrict__ out, long o_sb, long o_sh, float* __restrict__ part) {
   __shared__ float sm[WARPS], sl[WARPS];
   __shared__ float so[WARPS][D];
   const int split = blockIdx.x, splits = gridDim.x;
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = total[b];
+  const int n = total[b] + total_offset;
   const int c0 = split * chunk, c1 = min(n, c0 + chunk);
 
   float qv[4];
@@ -85,7 +87,9 @@ __global__ void __launch_bounds__(WARPS * 32)
     O += so[w][t] * f;
   }
   if (splits == 1) {
-    out[b * o_sb + h * o_sh + t] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+    float val = bf16_round(L > 0.f ? O / L : 0.f);
+    if (gate != nullptr) val *= sigmoidf_(__bfloat162float(gate[b * g_sb + h * g_sh + t]));
+    out[b * o_sb + h * o_sh + t] = __float2bfloat16_rn(val);
   } else {
     float* pp = part + ((long)bh * splits + split) * (D + 2);
     pp[2 + t] = O;
@@ -96,8 +100,9 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
 }
 
-__global__ void decode_combine_kernel(const float* __restrict__ part, int splits, int H, __nv_bfloat16* __restrict__ out,
-                                      long o_sb, long o_sh) {
+__global__ void decode_combine_kernel(const float* __restrict__ part, int splits, int H,
+                                      const __nv_bfloat16* __restrict__ gate, long g_sb, long g_sh,
+                                      __nv_bfloat16* __restrict__ out, long o_sb, long o_sh) {
   const int bh = blockIdx.x, b = bh / H, h = bh % H, t = threadIdx.x;
   const float* pp = part + (long)bh * splits * (D + 2);
   float mm = -INFINITY;
@@ -109,7 +114,30 @@ __global__ void decode_combine_kernel(const float* __restrict__ part, int splits
     L += pp[s * (D + 2) + 1] * f;
     O += pp[s * (D + 2) + 2 + t] * f;
   }
-  out[b * o_sb + h * o_sh + t] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+  float val = bf16_round(L > 0.f ? O / L : 0.f);
+  if (gate != nullptr) val *= sigmoidf_(__bfloat162float(gate[b * g_sb + h * g_sh + t]));
+  out[b * o_sb + h * o_sh + t] = __float2bfloat16_rn(val);
+}
+
+// The decode step's new key / value rows (from the fused gate|q|k|v projection output) into
+// the caches at position lengths[b]: one CTA per sequence, 16-byte copies.
+__global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ gqkv, long ld, int H, const int* __restrict__ lengths,
+                                 __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, long c_sb, long c_ss,
+                                 long c_sh) {
+  const int b = blockIdx.x;
+  const long pos = lengths[b];
+  for (int i = threadIdx.x; i < H * 16; i += blockDim.x) {
+    const int h = i >> 4, c = (i & 15) * 8;
+    const uint4 k = *reinterpret_cast<const uint4*>(gqkv + b * ld + (long)(2 * H + h) * D + c);
+    const uint4 v = *reinterpret_cast<const uint4*>(gqkv + b * ld + (long)(3 * H + h) * D + c);
+    *reinterpret_cast<uint4*>(kc + b * c_sb + pos * c_ss + h * c_sh + c) = k;
+    *reinterpret_cast<uint4*>(vc + b * c_sb + pos * c_ss + h * c_sh + c) = v;
+  }
+}
+
+int decode_splits(int B, int H, int S) {
+  const int sms = device_sm_count();
+  return std::max(1, std::min((S + 255) / 256, (2 * sms + B * H - 1) / std::max(1, B * H)));
 }
 
 }  // namespace
@@ -134,9 +162,7 @@ at::Tensor decode_attention(const at::Tensor& q, const at::Tensor& k_cache, cons
   const int B = (int)q.size(0), H = (int)q.size(1), S = (int)k_cache.size(1);
   auto out = at::empty({B, H, D}, q.options());
   // splits: enough CTAs to cover the GPU when B*H is small, one when the cache is short
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q.get_device());
-  int splits = std::max(1, std::min((S + 255) / 256, (2 * sms + B * H - 1) / std::max(1, B * H)));
+  const int splits = decode_splits(B, H, S);
   const int chunk = (S + splits - 1) / splits;
   at::Tensor part;
   if (splits > 1) part = at::empty({(long)B * H * splits * (D + 2)}, q.options().dtype(at::kFloat));
@@ -144,14 +170,57 @@ at::Tensor decode_attention(const at::Tensor& q, const at::Tensor& k_cache, cons
   decode_split_kernel<<<dim3(splits, B * H), WARPS * 32, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), q.stride(1),
       reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()),
-      k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), total.data_ptr<int>(), H, chunk, scale_log2,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), out.stride(1),
+      k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), total.data_ptr<int>(), 0, H, chunk, scale_log2,
+      nullptr, 0, 0, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), out.stride(1),
       splits > 1 ? part.data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (splits > 1) {
-    decode_combine_kernel<<<B * H, D, 0, stream>>>(part.data_ptr<float>(), splits, H,
+    decode_combine_kernel<<<B * H, D, 0, stream>>>(part.data_ptr<float>(), splits, H, nullptr, 0, 0,
                                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
                                                    out.stride(1));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  return out;
+}
+
+// The whole attention of one decode step from the fused projection output gqkv [B, 4H*128]
+// (gate, q, k, v heads; q and k rotated): appends k / v at lengths[b] in the caches, attends
+// over [0, lengths[b] + 1) and returns y = sigmoid(gate) * O as [B, H*128] bf16.
+at::Tensor decode_attention_gqkv(const at::Tensor& gqkv, int64_t H, const at::Tensor& k_cache,
+                                 const at::Tensor& v_cache, const at::Tensor& lengths) {
+  TORCH_CHECK(gqkv.is_cuda() && gqkv.dim() == 2 && gqkv.size(1) >= 4 * H * D && gqkv.stride(1) == 1 &&
+                  gqkv.scalar_type() == at::kBFloat16 && gqkv.stride(0) % 8 == 0,
+              "gqkv: [B, 4*H*128] bf16 with 16-byte aligned rows");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == H && k_cache.size(3) == D && k_cache.stride(3) == 1 &&
+                  v_cache.sizes() == k_cache.sizes() && v_cache.strides() == k_cache.strides() &&
+                  k_cache.scalar_type() == at::kBFloat16 && v_cache.scalar_type() == at::kBFloat16 &&
+                  k_cache.stride(2) % 8 == 0 && k_cache.stride(1) % 8 == 0 && k_cache.stride(0) % 8 == 0,
+              "caches: [B, S_max, H, 128] bf16 with matching, 16-byte aligned strides");
+  TORCH_CHECK(lengths.scalar_type() == at::kInt && lengths.numel() == gqkv.size(0), "lengths: int32 [B]");
+  c10::cuda::CUDAGuard guard(gqkv.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int B = (int)gqkv.size(0), S = (int)k_cache.size(1), h = (int)H;
+  const long ld = gqkv.stride(0);
+  auto kc = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  auto vc = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  const auto* g = reinterpret_cast<const __nv_bfloat16*>(gqkv.data_ptr());
+  kv_append_kernel<<<B, 256, 0, stream>>>(g, ld, h, lengths.data_ptr<int>(), kc, vc, k_cache.stride(0),
+                                          k_cache.stride(1), k_cache.stride(2));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  auto out = at::empty({B, h * D}, gqkv.options());
+  const int splits = decode_splits(B, h, S);
+  const int chunk = (S + splits - 1) / splits;
+  at::Tensor part;
+  if (splits > 1) part = at::empty({(long)B * h * splits * (D + 2)}, gqkv.options().dtype(at::kFloat));
+  const float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  decode_split_kernel<<<dim3(splits, B * h), WARPS * 32, 0, stream>>>(
+      g + (long)h * D, ld, D, kc, vc, k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+      lengths.data_ptr<int>(), 1, h, chunk, scale_log2, g, ld, D, o, out.stride(0), D,
+      splits > 1 ? part.data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (splits > 1) {
+    decode_combine_kernel<<<B * h, D, 0, stream>>>(part.data_ptr<float>(), splits, h, g, ld, D, o, out.stride(0), D);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   return out;

@@ -122,6 +122,37 @@ def decode_step(model: nn.Module, carry, last_tokens: Tensor, cache, cache_lengt
     return model(carry=carry, batch=batch)[-1][:, -1]
 
 
+class DecodeGraph:
+    """The decode step (all ``batch_size`` slots, one token each) captured in one CUDA graph.
+
+    The step's work is a fixed sequence of device operations on static shapes (embedding,
+    per module call and layer the RMSNorm / GEMM / decode-attention kernels, the LM-head GEMM),
+    so it is captured once per cache and replayed for every generated token; the per-step
+    inputs (last tokens, cache lengths) are copied into static buffers. Capture writes junk
+    keys / values at position 0 of every slot, so it must happen before any prompt is
+    prefilled into the cache.
+    """
+
+    def __init__(self, model: nn.Module, carry, cache, batch_size: int, device: torch.device, warmup: int = 2):
+        self.tokens = torch.zeros(batch_size, dtype=torch.long, device=device)
+        self.lengths = torch.zeros(batch_size, dtype=torch.int32, device=device)
+        stream = torch.cuda.Stream(device=device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                decode_step(model, carry, self.tokens, cache, self.lengths)
+        torch.cuda.current_stream(device).wait_stream(stream)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.logits = decode_step(model, carry, self.tokens, cache, self.lengths)
+
+    def __call__(self, last_tokens: Tensor, cache_lengths: Tensor) -> Tensor:
+        self.tokens.copy_(last_tokens, non_blocking=True)
+        self.lengths.copy_(cache_lengths, non_blocking=True)
+        self.graph.replay()
+        return self.logits
+
+
 def _slot_view(cache, i: int):
     return torch.utils._pytree.tree_map(lambda x: x[i:i + 1] if isinstance(x, Tensor) else x, cache)
 
@@ -129,11 +160,18 @@ def _slot_view(cache, i: int):
 @torch.inference_mode()
 def generate_tokens(model: nn.Module, carry, prompts: Iterator[tuple[int, np.ndarray]], max_tokens: int,
                     max_generation: int, batch_size: int, stop_token: int, temp: float = 0.0,
-                    device: Optional[torch.device] = None) -> Generator[tuple[int, np.ndarray], None, None]:
-    """Continuous-batching generation over token prompts; yields ``(prompt_id, generated_ids)``."""
+                    device: Optional[torch.device] = None,
+                    use_cuda_graph: bool = True) -> Generator[tuple[int, np.ndarray], None, None]:
+    """Continuous-batching generation over token prompts; yields ``(prompt_id, generated_ids)``.
+
+    On a CUDA device with bf16 weights the decode step runs as one captured CUDA graph
+    (``DecodeGraph``)."""
     device = device or next(model.parameters()).device
     dtype = next(model.parameters()).dtype
     cache = model.create_cache(max_batch_size=batch_size, max_seq_len=max_tokens, dtype=dtype, device=device)
+    graphed = None
+    if use_cuda_graph and device.type == "cuda" and dtype == torch.bfloat16:
+        graphed = DecodeGraph(model, carry, cache, batch_size, device)  # before any prefill (see DecodeGraph)
     lengths = torch.zeros(batch_size, dtype=torch.int32, device=device)
     last = torch.zeros(batch_size, dtype=torch.long, device=device)
     generated = np.zeros((batch_size, max_tokens), dtype=np.int64)
@@ -170,7 +208,7 @@ def generate_tokens(model: nn.Module, carry, prompts: Iterator[tuple[int, np.nda
             stopped[i] = first == stop_token or g_len[i] >= max_tokens
             pending_id, pending = yield from next_prompt()
         if not stopped.all():
-            logits = decode_step(model, carry, last, cache, lengths)
+            logits = graphed(last, lengths) if graphed is not None else decode_step(model, carry, last, cache, lengths)
             last = sample(logits, temp)
             lengths.add_(1).clamp_max_(max_tokens - 1)
             active = ~stopped

@@ -82,7 +82,13 @@ class LMHead(nn.Module):
         new_carry, hidden = self.model(carry, hidden, **passthrough, **kwargs)
 
         if "labels" not in batch:
-            return new_carry, F.linear(hidden, self.lm_head.weight.to(hidden.dtype))
+            w = self.lm_head.weight
+            if fused_path(hidden) and hidden.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 \
+                    and w.shape[0] % 32 == 0:
+                from ..ops import gemm as G  # tcgen05 GEMM (inference logits)
+                flat = hidden.reshape(-1, hidden.shape[-1]).contiguous()
+                return new_carry, G.linear(flat, w).view(*hidden.shape[:-1], w.shape[0])
+            return new_carry, F.linear(hidden, w.to(hidden.dtype))
 
         labels = batch["labels"]
         valid = labels != IGNORE_LABEL_ID

@@ -132,9 +132,15 @@ class Transformer(nn.Module):
     def forward(self, x: Tensor, cache: Optional[list[Cache]] = None, injection: Optional[Tensor] = None,
                 **seq_info) -> Tensor:
         """Run the stack on ``x (+ injection)``; ``seq_info`` carries packing metadata."""
-        if cache is None and fused_path(x if injection is None else injection):
+        if fused_path(x if injection is None else injection):
             from ..ops import block as fused_block
-            return fused_block.stack_forward(self, x, injection, seq_info)
+            if cache is None:
+                return fused_block.stack_forward(self, x, injection, seq_info)
+            if not torch.is_grad_enabled() and seq_info.get("position_ids") is not None:
+                out = fused_block.stack_forward_cached(self, x, injection, cache, seq_info.get("cache_lengths"),
+                                                       seq_info["position_ids"])
+                if out is not None:
+                    return out
 
         if injection is not None:
             x = x + injection

@@ -172,3 +172,73 @@ def stack_forward(stack, x: Tensor, injection: Tensor | None, seq_info: dict) ->
                                     m.gate_up_proj.weight, m.down_proj.weight, packed, rope, a.num_heads,
                                     cfg.norm_eps, causal, train)
     return FinalNorm.apply(x, cfg.norm_eps)
+
+
+def stack_forward_cached(stack, x: Tensor, injection: Tensor | None, cache: list, cache_lengths,
+                         position_ids: Tensor) -> Tensor | None:
+    """Inference forward of a pre-norm ``Transformer`` stack against static KV caches, on the
+    framework's kernels (reference models/layers.py:129-168 with ``flash_attn_with_kvcache``,
+    simple_inference_engine.py:105-112).
+
+    Two shapes of call run here; anything else returns ``None`` (the caller then uses the
+    torch reference path):
+
+    * decode: ``x [B, 1, h]``, ``cache_lengths`` a ``[B]`` tensor. Per layer: RMSNorm kernel,
+      tcgen05 gqkv GEMM with the RoPE epilogue at positions ``cache_lengths``, one decode
+      attention call that appends the step's keys / values to the caches, attends over
+      ``[0, cache_lengths + 1)`` and applies the sigmoid gate, then the o_proj GEMM with the
+      residual epilogue, RMSNorm, the gate/up GEMM with the SwiGLU epilogue and the down GEMM
+      with the residual epilogue;
+    * prefill of one prompt into an empty cache: ``x [1, L, h]``, ``cache_lengths == 0``. The
+      same GEMMs, the prompt's keys / values copied into the caches, and the tcgen05 PrefixLM
+      forward over the prompt (bidirectional; causal for a causal stack).
+
+    Every launch is a device-side operation on static shapes, so a decode step can be captured
+    in a CUDA graph.
+    """
+    cfg = stack.config
+    if cfg.norm_type != "pre" or cfg.head_dim != 128 or not hasattr(stack, "rotary_emb"):
+        return None
+    ref = injection if injection is not None else x
+    if ref.dim() != 3:
+        return None
+    B, S, hidden = ref.shape
+    decode = S == 1 and isinstance(cache_lengths, Tensor) and cache_lengths.numel() == B
+    prefill = B == 1 and isinstance(cache_lengths, int) and cache_lengths == 0
+    if not (decode or prefill):
+        return None
+    cos, sin = rope_half_tables(stack.rotary_emb)
+    causal = cfg.attn_type == "causal"
+    T = B * S
+    if x.dim() == 1:  # broadcast initial state (zL_init)
+        x = x.to(ref.dtype).expand(T, hidden).contiguous()
+    else:
+        x = x.reshape(T, hidden)
+    inj = injection.reshape(T, hidden).contiguous() if injection is not None else None
+    positions = position_ids.reshape(-1).to(torch.int32).contiguous()
+    if decode:
+        lengths = cache_lengths.to(device=x.device, dtype=torch.int32).contiguous()
+    else:
+        cu = torch.tensor([0, S], dtype=torch.int32, device=x.device)
+        pl = torch.tensor([0 if causal else S], dtype=torch.int32, device=x.device)
+        packed = PackedSeq(positions, cu, pl)
+        sched = packed.schedule(causal)
+    for i, layer in enumerate(stack.layers):
+        a, m = layer.attn, layer.mlp
+        H = a.num_heads
+        c = cache[i]
+        xn, _, s = rmsnorm(x, cfg.norm_eps, inj if i == 0 else None)
+        gqkv = G.linear_rope(xn, a.gqkv_proj.weight, positions, cos, sin, hidden, 3 * hidden)
+        if decode:
+            y = cuda().decode_attention_gqkv(gqkv, H, c.keys, c.values, lengths)
+        else:
+            heads = gqkv.view(S, 4, H, 128)
+            c.keys[0, :S].copy_(heads[:, 2])
+            c.values[0, :S].copy_(heads[:, 3])
+            _, y, _ = attention_fwd(gqkv, H, sched)
+        x1 = G.linear(y, a.o_proj.weight, residual=s)
+        xn2, _, _ = rmsnorm(x1, cfg.norm_eps)
+        _, h = G.linear_swiglu(xn2, m.gate_up_proj.weight)
+        x = G.linear(h, m.down_proj.weight, residual=x1)
+    out, _, _ = rmsnorm(x, cfg.norm_eps)
+    return out.view(B, S, hidden)
