@@ -33,6 +33,10 @@ at::Tensor decode_attention(const at::Tensor& q, const at::Tensor& k_cache, cons
                             const at::Tensor& total);
 at::Tensor decode_attention_gqkv(const at::Tensor& gqkv, int64_t H, const at::Tensor& k_cache,
                                  const at::Tensor& v_cache, const at::Tensor& lengths);
+void skinny_linear(const at::Tensor& x, const at::Tensor& w, int64_t epi, const at::Tensor& out,
+                   const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& positions,
+                   const c10::optional<at::Tensor>& cos_tab, const c10::optional<at::Tensor>& sin_tab,
+                   int64_t rope_begin, int64_t rope_end, int64_t pair_offset);
 void attn_bwd_set_profile(bool enabled);
 at::Tensor attn_bwd_phase_counters(bool reset);
 void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
@@ -73,6 +77,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &hrm::attn_bwd);
   m.def("attn_bwd_tc", &hrm::attn_bwd_tc, "tcgen05 PrefixLM attention backward");
   m.def("decode_attention", &hrm::decode_attention, "split-KV decode attention against a static KV cache");
+  m.def("skinny_linear", &hrm::skinny_linear, "small-M (decode) linear layer with fused epilogues");
   m.def("decode_attention_gqkv", &hrm::decode_attention_gqkv,
         "decode step attention from the fused projection: KV append, split-KV attention, sigmoid gate");
   m.def("sample_tokens", &hrm::sample_tokens, "greedy / Gumbel-max token sampling (fused, one CTA per row)");

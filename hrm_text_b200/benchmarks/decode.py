@@ -67,6 +67,27 @@ def run_ours(args) -> dict:
     return {"impl": "ours", "ms_per_step": ms}
 
 
+def _import_with_py313_generator(name: str):
+    """Import a reference module whose annotations use Python 3.13's two-argument
+    ``typing.Generator[Y, S]`` (the reference targets 3.13; this interpreter is 3.12): while it
+    is imported, ``typing.Generator`` accepts two arguments and fills in the default return
+    type ``None``. Only annotation objects are affected, not the module's computation."""
+    import importlib
+    import typing
+    original = typing.Generator
+
+    class _Generator:
+        def __class_getitem__(cls, item):
+            item = item if isinstance(item, tuple) else (item,)
+            return original[item + (None,) * (3 - len(item))]
+
+    typing.Generator = _Generator
+    try:
+        return importlib.import_module(name)
+    finally:
+        typing.Generator = original
+
+
 def run_reference(args) -> dict:
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     ref = os.path.join(root, "baseline", "_ref")
@@ -77,7 +98,7 @@ def run_reference(args) -> dict:
     if os.path.exists("/usr/bin/g++"):
         os.environ["CXX"] = "/usr/bin/g++"  # Inductor's CPU codegen needs an OpenMP-capable g++
     _install_import_shims()
-    import simple_inference_engine as sie  # the reference's module
+    sie = _import_with_py313_generator("simple_inference_engine")  # the reference's module
     from utils.functions import load_model_class
     arch = ref_arch(args.size)
     cfg = arch | {"vocab_size": VOCAB, "max_seq_len": MAX_SEQ_LEN}

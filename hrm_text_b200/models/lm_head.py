@@ -87,7 +87,7 @@ class LMHead(nn.Module):
                     and w.shape[0] % 32 == 0:
                 from ..ops import gemm as G  # tcgen05 GEMM (inference logits)
                 flat = hidden.reshape(-1, hidden.shape[-1]).contiguous()
-                return new_carry, G.linear(flat, w).view(*hidden.shape[:-1], w.shape[0])
+                return new_carry, G.infer_linear(flat, w).view(*hidden.shape[:-1], w.shape[0])
             return new_carry, F.linear(hidden, w.to(hidden.dtype))
 
         labels = batch["labels"]

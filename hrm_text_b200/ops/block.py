@@ -184,7 +184,8 @@ def stack_forward_cached(stack, x: Tensor, injection: Tensor | None, cache: list
     torch reference path):
 
     * decode: ``x [B, 1, h]``, ``cache_lengths`` a ``[B]`` tensor. Per layer: RMSNorm kernel,
-      tcgen05 gqkv GEMM with the RoPE epilogue at positions ``cache_lengths``, one decode
+      gqkv projection with RoPE at positions ``cache_lengths`` (the small-M kernel of
+      skinny_gemm.cu for B <= 32, the tcgen05 GEMM above that), one decode
       attention call that appends the step's keys / values to the caches, attends over
       ``[0, cache_lengths + 1)`` and applies the sigmoid gate, then the o_proj GEMM with the
       residual epilogue, RMSNorm, the gate/up GEMM with the SwiGLU epilogue and the down GEMM
@@ -228,7 +229,7 @@ def stack_forward_cached(stack, x: Tensor, injection: Tensor | None, cache: list
         H = a.num_heads
         c = cache[i]
         xn, _, s = rmsnorm(x, cfg.norm_eps, inj if i == 0 else None)
-        gqkv = G.linear_rope(xn, a.gqkv_proj.weight, positions, cos, sin, hidden, 3 * hidden)
+        gqkv = G.infer_linear_rope(xn, a.gqkv_proj.weight, positions, cos, sin, hidden, 3 * hidden)
         if decode:
             y = cuda().decode_attention_gqkv(gqkv, H, c.keys, c.values, lengths)
         else:
@@ -236,9 +237,9 @@ def stack_forward_cached(stack, x: Tensor, injection: Tensor | None, cache: list
             c.keys[0, :S].copy_(heads[:, 2])
             c.values[0, :S].copy_(heads[:, 3])
             _, y, _ = attention_fwd(gqkv, H, sched)
-        x1 = G.linear(y, a.o_proj.weight, residual=s)
+        x1 = G.infer_linear(y, a.o_proj.weight, residual=s)
         xn2, _, _ = rmsnorm(x1, cfg.norm_eps)
-        _, h = G.linear_swiglu(xn2, m.gate_up_proj.weight)
-        x = G.linear(h, m.down_proj.weight, residual=x1)
+        h = G.infer_swiglu(xn2, m.gate_up_proj.weight)
+        x = G.infer_linear(h, m.down_proj.weight, residual=x1)
     out, _, _ = rmsnorm(x, cfg.norm_eps)
     return out.view(B, S, hidden)

@@ -136,6 +136,48 @@ def lm_head_ce_dlogits(x: Tensor, w_chunk: Tensor, labels: Tensor, lse: Tensor, 
 
 
 # ---------------------------------------------------------------------------------------
+# inference: the same layers for any M, with a small-M kernel for decode steps (M <= 32)
+# ---------------------------------------------------------------------------------------
+SKINNY_MAX_M = 32
+
+
+def _skinny(x: Tensor) -> bool:
+    return x.shape[0] <= SKINNY_MAX_M and x.stride(1) == 1 and x.stride(0) % 8 == 0
+
+
+def infer_linear(x: Tensor, w: Tensor, residual: Optional[Tensor] = None) -> Tensor:
+    """``x @ w.T (+ residual)``: the small-M kernel for M <= 32, else the tcgen05 GEMM."""
+    _check(x, w)
+    if not _skinny(x):
+        return linear(x, w, residual=residual)
+    out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.bfloat16, device=x.device)
+    cuda().skinny_linear(x, w, EPI_RESIDUAL if residual is not None else EPI_STORE, out, residual, None, None, None,
+                         0, 0, 0)
+    return out
+
+
+def infer_linear_rope(x: Tensor, w: Tensor, positions: Tensor, cos: Tensor, sin: Tensor, rope_begin: int,
+                      rope_end: int) -> Tensor:
+    _check(x, w)
+    if not _skinny(x):
+        return linear_rope(x, w, positions, cos, sin, rope_begin, rope_end)
+    out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.bfloat16, device=x.device)
+    cuda().skinny_linear(x, w, EPI_ROPE, out, None, positions, cos, sin, rope_begin, rope_end, 0)
+    return out
+
+
+def infer_swiglu(x: Tensor, w: Tensor) -> Tensor:
+    """``silu(x @ gate.T) * (x @ up.T)`` for ``w = [gate; up]`` (only ``h`` is produced)."""
+    _check(x, w)
+    if not _skinny(x):
+        return linear_swiglu(x, w)[1]
+    inter = w.shape[0] // 2
+    h = torch.empty((x.shape[0], inter), dtype=torch.bfloat16, device=x.device)
+    cuda().skinny_linear(x, w, EPI_SWIGLU, h, None, None, None, None, 0, 0, inter)
+    return h
+
+
+# ---------------------------------------------------------------------------------------
 # fused-collective variants (multi-GPU sharding engine; see hrm_text_b200.parallel.fused)
 # ---------------------------------------------------------------------------------------
 def linear_rope_f1(x: Tensor, w: Tensor, positions: Tensor, cos: Tensor, sin: Tensor, rope_begin: int,

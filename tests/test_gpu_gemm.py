@@ -101,3 +101,34 @@ def test_lm_head_cross_entropy(cuda_device, T, H, V, chunk):
     (ref * 0.01).backward()
     assert_close(x.grad, xr.grad, 3e-2, "d hidden")
     assert_close(w.grad, wr.grad, 3e-2, "d weight")
+
+
+@pytest.mark.parametrize("M", [1, 7, 32])
+def test_skinny_linear_epilogues(cuda_device, M):
+    """The small-M (decode) kernel against fp32 torch for every epilogue it implements."""
+    from hrm_text_b200.models.layers import rope_tables
+    from hrm_text_b200.ops import gemm as G
+    torch.manual_seed(7)
+    H, hidden, inter = 2, 256, 1536
+    x = torch.randn(M, hidden, device=cuda_device).bfloat16()
+    w = (torch.randn(4 * hidden, hidden, device=cuda_device) / 16).bfloat16()
+    ref = (x.float() @ w.float().T).bfloat16().float()
+    r = torch.randn(M, 4 * hidden, device=cuda_device).bfloat16()
+    assert_close(G.infer_linear(x, w), ref, 1e-2, "store")
+    assert_close(G.infer_linear(x, w, residual=r), ref + r.float(), 1e-2, "residual")
+    cos, sin = rope_tables(128, 64, 10000.0, device=cuda_device)
+    pos = torch.randint(0, 64, (M,), device=cuda_device, dtype=torch.int32)
+    out = G.infer_linear_rope(x, w, pos, cos[:, :64].contiguous(), sin[:, :64].contiguous(), hidden, 3 * hidden)
+    heads = ref.view(M, 4 * H, 128)
+    c, s = cos[pos.long()][:, None], sin[pos.long()][:, None]
+    rot = torch.cat([-heads[..., 64:], heads[..., :64]], -1)
+    want = heads.clone()
+    want[:, H:3 * H] = heads[:, H:3 * H] * c + rot[:, H:3 * H] * s
+    assert_close(out, want.view(M, -1), 1e-2, "rope")
+    wg = (torch.randn(2 * inter, hidden, device=cuda_device) / 16).bfloat16()
+    gu = (x.float() @ wg.float().T).bfloat16().float()
+    g, u = gu[:, :inter], gu[:, inter:]
+    assert_close(G.infer_swiglu(x, wg), torch.nn.functional.silu(g) * u, 2e-2, "swiglu")
+    wd = (torch.randn(hidden, inter, device=cuda_device) / 40).bfloat16()  # K > one 1024-column chunk
+    h = torch.randn(M, inter, device=cuda_device).bfloat16()
+    assert_close(G.infer_linear(h, wd), h.float() @ wd.float().T, 1e-2, "long K")
