@@ -9,7 +9,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
           const c10::optional<at::Tensor>& sin_tab, int64_t rope_begin, int64_t rope_end, int64_t pair_offset,
           const c10::optional<at::Tensor>& labels, const c10::optional<at::Tensor>& ce_max,
           const c10::optional<at::Tensor>& ce_sum, const c10::optional<at::Tensor>& ce_arg,
-          const c10::optional<at::Tensor>& ce_tgt, bool stream_k);
+          const c10::optional<at::Tensor>& ce_tgt, bool stream_k, int64_t splitk);
 at::Tensor encode_shard_maps(const std::vector<int64_t>& shard_addrs, int64_t shard_rows, int64_t cols);
 void gemm_f1(const at::Tensor& x, const at::Tensor& w, int64_t M, int64_t N, int64_t K, int64_t epi,
              const at::Tensor& out, const c10::optional<at::Tensor>& out2, const c10::optional<at::Tensor>& positions,
@@ -33,10 +33,10 @@ at::Tensor decode_attention(const at::Tensor& q, const at::Tensor& k_cache, cons
                             const at::Tensor& total);
 at::Tensor decode_attention_gqkv(const at::Tensor& gqkv, int64_t H, const at::Tensor& k_cache,
                                  const at::Tensor& v_cache, const at::Tensor& lengths);
-void skinny_linear(const at::Tensor& x, const at::Tensor& w, int64_t epi, const at::Tensor& out,
-                   const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& positions,
-                   const c10::optional<at::Tensor>& cos_tab, const c10::optional<at::Tensor>& sin_tab,
-                   int64_t rope_begin, int64_t rope_end, int64_t pair_offset);
+void decode_linear_finish(const at::Tensor& acc, int64_t epi, const at::Tensor& out,
+                          const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& positions,
+                          const c10::optional<at::Tensor>& cos_tab, const c10::optional<at::Tensor>& sin_tab,
+                          int64_t rope_begin, int64_t rope_end, int64_t pair_offset);
 void attn_bwd_set_profile(bool enabled);
 at::Tensor attn_bwd_phase_counters(bool reset);
 void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const at::Tensor& out,
@@ -77,7 +77,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &hrm::attn_bwd);
   m.def("attn_bwd_tc", &hrm::attn_bwd_tc, "tcgen05 PrefixLM attention backward");
   m.def("decode_attention", &hrm::decode_attention, "split-KV decode attention against a static KV cache");
-  m.def("skinny_linear", &hrm::skinny_linear, "small-M (decode) linear layer with fused epilogues");
+  m.def("decode_linear_finish", &hrm::decode_linear_finish,
+        "bf16 output of a split-K decode-step linear layer with the RoPE / SwiGLU / residual epilogues");
   m.def("decode_attention_gqkv", &hrm::decode_attention_gqkv,
         "decode step attention from the fused projection: KV append, split-KV attention, sigmoid gate");
   m.def("sample_tokens", &hrm::sample_tokens, "greedy / Gumbel-max token sampling (fused, one CTA per row)");

@@ -22,7 +22,8 @@ namespace hrm {
 namespace {
 
 constexpr int D = 128;
-constexpr int WARPS = 4;
+constexpr int WARPS = 8;
+constexpr int KG = 4;  // keys per warp iteration: their loads are in flight together
 
 __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
   const uint2 w = *reinterpret_cast<const uint2*>(p);
@@ -51,19 +52,39 @@ __global__ void __launch_bounds__(WARPS * 32)
   float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
   const __nv_bfloat16* kb = kc + b * c_sb + h * c_sh + lane * 4;
   const __nv_bfloat16* vb = vc + b * c_sb + h * c_sh + lane * 4;
-  for (int j = c0 + warp; j < c1; j += WARPS) {
-    float kv[4], vv[4];
-    load4(kb + (long)j * c_ss, kv);
-    load4(vb + (long)j * c_ss, vv);
-    float s = qv[0] * kv[0] + qv[1] * kv[1] + qv[2] * kv[2] + qv[3] * kv[3];
+  // KG keys per iteration: all their K / V rows are requested before any is used (decoding is
+  // bound by the latency of these loads, not by arithmetic)
+  for (int j0 = c0 + warp * KG; j0 < c1; j0 += WARPS * KG) {
+    float kv[KG][4], vv[KG][4], sc[KG];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    const float m_new = fmaxf(m, s);
-    const float alpha = fast_exp2(m - m_new);  // 0 on the first key (m = -inf)
-    const float p = fast_exp2(s - m_new);
-    l = l * alpha + p;
+    for (int u = 0; u < KG; ++u) {
+      const int j = min(j0 + u, c1 - 1);  // clamped: the duplicate is masked below
+      load4(kb + (long)j * c_ss, kv[u]);
+      load4(vb + (long)j * c_ss, vv[u]);
+    }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) o[i] = o[i] * alpha + p * vv[i];
+    for (int u = 0; u < KG; ++u) sc[u] = qv[0] * kv[u][0] + qv[1] * kv[u][1] + qv[2] * kv[u][2] + qv[3] * kv[u][3];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int u = 0; u < KG; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+    float m_new = m;
+#pragma unroll
+    for (int u = 0; u < KG; ++u) {
+      if (j0 + u >= c1) sc[u] = -INFINITY;
+      m_new = fmaxf(m_new, sc[u]);
+    }
+    const float alpha = fast_exp2(m - m_new);  // 0 on the first keys (m = -inf)
+    l *= alpha;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] *= alpha;
+#pragma unroll
+    for (int u = 0; u < KG; ++u) {
+      const float p = fast_exp2(sc[u] - m_new);  // 0 for masked keys
+      l += p;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = fmaf(p, vv[u][i], o[i]);
+    }
     m = m_new;
   }
   if (lane == 0) {
@@ -73,8 +94,9 @@ __global__ void __launch_bounds__(WARPS * 32)
 #pragma unroll
   for (int i = 0; i < 4; ++i) so[warp][lane * 4 + i] = o[i];
   __syncthreads();
-  // merge the warps: thread t owns dim t
+  // merge the warps: thread t < 128 owns dim t
   const int t = threadIdx.x;
+  if (t >= D) return;
   float mm = -INFINITY;
 #pragma unroll
   for (int w = 0; w < WARPS; ++w) mm = fmaxf(mm, sm[w]);
@@ -135,9 +157,12 @@ __global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ gqkv, long ld
   }
 }
 
+// Key ranges per (sequence, head): about 128 cache positions each (16 per warp), so that the
+// loads of all warps together keep enough bytes in flight; a combine pass merges the ranges.
 int decode_splits(int B, int H, int S) {
-  const int sms = device_sm_count();
-  return std::max(1, std::min((S + 255) / 256, (2 * sms + B * H - 1) / std::max(1, B * H)));
+  (void)B;
+  (void)H;
+  return std::max(1, std::min(64, (S + 127) / 128));
 }
 
 }  // namespace

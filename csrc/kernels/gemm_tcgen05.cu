@@ -924,7 +924,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
           const c10::optional<at::Tensor>& sin_tab, int64_t rope_begin, int64_t rope_end, int64_t pair_offset,
           const c10::optional<at::Tensor>& labels, const c10::optional<at::Tensor>& ce_max,
           const c10::optional<at::Tensor>& ce_sum, const c10::optional<at::Tensor>& ce_arg,
-          const c10::optional<at::Tensor>& ce_tgt, bool stream_k) {
+          const c10::optional<at::Tensor>& ce_tgt, bool stream_k, int64_t splitk) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm: row-major 2D operands");
   TORCH_CHECK(N % 32 == 0, "gemm: N must be a multiple of 32");
@@ -970,6 +970,8 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
       return v == nullptr || std::string(v) != "0";
     }();
     if (!chunked) args.splitk = 1;
+    // an explicit split (decode-step GEMMs: a few rows, K spread over many CTAs)
+    if (splitk > 0) args.splitk = (int)std::max<int64_t>(1, std::min<int64_t>(splitk, (K + BK - 1) / BK));
   }
 
   CUtensorMap ma = a_mn ? make_map(a, M, K, a.stride(0), 64, 64) : make_map(a, K, M, a.stride(0), 64, 128);

@@ -76,12 +76,15 @@ def _import_with_py313_generator(name: str):
     import typing
     original = typing.Generator
 
-    class _Generator:
-        def __class_getitem__(cls, item):
+    class _GeneratorAlias:
+        def __getitem__(self, item):
             item = item if isinstance(item, tuple) else (item,)
             return original[item + (None,) * (3 - len(item))]
 
-    typing.Generator = _Generator
+        def __getattr__(self, name):  # everything else is typing.Generator's
+            return getattr(original, name)
+
+    typing.Generator = _GeneratorAlias()
     try:
         return importlib.import_module(name)
     finally:

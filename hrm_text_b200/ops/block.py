@@ -184,8 +184,8 @@ def stack_forward_cached(stack, x: Tensor, injection: Tensor | None, cache: list
     torch reference path):
 
     * decode: ``x [B, 1, h]``, ``cache_lengths`` a ``[B]`` tensor. Per layer: RMSNorm kernel,
-      gqkv projection with RoPE at positions ``cache_lengths`` (the small-M kernel of
-      skinny_gemm.cu for B <= 32, the tcgen05 GEMM above that), one decode
+      gqkv projection with RoPE at positions ``cache_lengths`` (tcgen05 GEMM in split-K mode
+      plus the epilogue kernel of skinny_gemm.cu), one decode
       attention call that appends the step's keys / values to the caches, attends over
       ``[0, cache_lengths + 1)`` and applies the sigmoid gate, then the o_proj GEMM with the
       residual epilogue, RMSNorm, the gate/up GEMM with the SwiGLU epilogue and the down GEMM

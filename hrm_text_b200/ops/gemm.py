@@ -30,9 +30,9 @@ def _check(*tensors: Tensor) -> None:
 
 def _gemm(a, a_mn, b, b_mn, M, N, K, epi, out, out2=None, residual=None, aux=None, positions=None, cos=None,
           sin=None, rope_begin=0, rope_end=0, pair_offset=0, labels=None, ce_max=None, ce_sum=None, ce_arg=None,
-          ce_tgt=None, stream_k=False):
+          ce_tgt=None, stream_k=False, splitk=0):
     cuda().gemm(a, a_mn, b, b_mn, M, N, K, epi, out, out2, residual, aux, positions, cos, sin, rope_begin, rope_end,
-                pair_offset, labels, ce_max, ce_sum, ce_arg, ce_tgt, stream_k)
+                pair_offset, labels, ce_max, ce_sum, ce_arg, ce_tgt, stream_k, splitk)
 
 
 def linear(x: Tensor, w: Tensor, out: Optional[Tensor] = None, residual: Optional[Tensor] = None) -> Tensor:
@@ -136,44 +136,64 @@ def lm_head_ce_dlogits(x: Tensor, w_chunk: Tensor, labels: Tensor, lse: Tensor, 
 
 
 # ---------------------------------------------------------------------------------------
-# inference: the same layers for any M, with a small-M kernel for decode steps (M <= 32)
+# inference: the same layers for any M; decode steps (M <= 128) run the tcgen05 GEMM in
+# split-K mode (K spread over all SMs, fp32 partials added into a zeroed [M, N] buffer) and a
+# finishing kernel with the epilogue (csrc/kernels/skinny_gemm.cu)
 # ---------------------------------------------------------------------------------------
-SKINNY_MAX_M = 32
+DECODE_MAX_M = 128
+_SM_COUNT: dict = {}
 
 
-def _skinny(x: Tensor) -> bool:
-    return x.shape[0] <= SKINNY_MAX_M and x.stride(1) == 1 and x.stride(0) % 8 == 0
+def _decode_gemm(x: Tensor, w: Tensor) -> Tensor:
+    M, K = x.shape
+    N = w.shape[0]
+    dev = x.device
+    sms = _SM_COUNT.get(dev)
+    if sms is None:
+        sms = _SM_COUNT[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
+    tiles = -(-N // 256)
+    split = max(1, min(-(-K // 64), round(2 * sms / tiles)))
+    acc = torch.zeros((M, N), dtype=torch.float32, device=dev)
+    _gemm(x, False, w, False, M, N, K, EPI_F32ADD, acc, stream_k=True, splitk=split)
+    return acc
+
+
+def _decode_path(x: Tensor) -> bool:
+    return x.shape[0] <= DECODE_MAX_M
 
 
 def infer_linear(x: Tensor, w: Tensor, residual: Optional[Tensor] = None) -> Tensor:
-    """``x @ w.T (+ residual)``: the small-M kernel for M <= 32, else the tcgen05 GEMM."""
+    """``x @ w.T (+ residual)`` for inference."""
     _check(x, w)
-    if not _skinny(x):
+    if not _decode_path(x):
         return linear(x, w, residual=residual)
+    acc = _decode_gemm(x, w)
     out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.bfloat16, device=x.device)
-    cuda().skinny_linear(x, w, EPI_RESIDUAL if residual is not None else EPI_STORE, out, residual, None, None, None,
-                         0, 0, 0)
+    cuda().decode_linear_finish(acc, EPI_RESIDUAL if residual is not None else EPI_STORE, out, residual, None, None,
+                                None, 0, 0, 0)
     return out
 
 
 def infer_linear_rope(x: Tensor, w: Tensor, positions: Tensor, cos: Tensor, sin: Tensor, rope_begin: int,
                       rope_end: int) -> Tensor:
     _check(x, w)
-    if not _skinny(x):
+    if not _decode_path(x):
         return linear_rope(x, w, positions, cos, sin, rope_begin, rope_end)
+    acc = _decode_gemm(x, w)
     out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.bfloat16, device=x.device)
-    cuda().skinny_linear(x, w, EPI_ROPE, out, None, positions, cos, sin, rope_begin, rope_end, 0)
+    cuda().decode_linear_finish(acc, EPI_ROPE, out, None, positions, cos, sin, rope_begin, rope_end, 0)
     return out
 
 
 def infer_swiglu(x: Tensor, w: Tensor) -> Tensor:
     """``silu(x @ gate.T) * (x @ up.T)`` for ``w = [gate; up]`` (only ``h`` is produced)."""
     _check(x, w)
-    if not _skinny(x):
+    if not _decode_path(x):
         return linear_swiglu(x, w)[1]
     inter = w.shape[0] // 2
+    acc = _decode_gemm(x, w)
     h = torch.empty((x.shape[0], inter), dtype=torch.bfloat16, device=x.device)
-    cuda().skinny_linear(x, w, EPI_SWIGLU, h, None, None, None, None, 0, 0, inter)
+    cuda().decode_linear_finish(acc, EPI_SWIGLU, h, None, None, None, None, 0, 0, inter)
     return h
 
 

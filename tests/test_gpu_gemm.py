@@ -103,9 +103,9 @@ def test_lm_head_cross_entropy(cuda_device, T, H, V, chunk):
     assert_close(w.grad, wr.grad, 3e-2, "d weight")
 
 
-@pytest.mark.parametrize("M", [1, 7, 32])
-def test_skinny_linear_epilogues(cuda_device, M):
-    """The small-M (decode) kernel against fp32 torch for every epilogue it implements."""
+@pytest.mark.parametrize("M", [1, 7, 32, 128])
+def test_decode_linear_epilogues(cuda_device, M):
+    """Decode-step linear layers (split-K tcgen05 GEMM + epilogue kernel) against fp32 torch."""
     from hrm_text_b200.models.layers import rope_tables
     from hrm_text_b200.ops import gemm as G
     torch.manual_seed(7)
@@ -129,6 +129,6 @@ def test_skinny_linear_epilogues(cuda_device, M):
     gu = (x.float() @ wg.float().T).bfloat16().float()
     g, u = gu[:, :inter], gu[:, inter:]
     assert_close(G.infer_swiglu(x, wg), torch.nn.functional.silu(g) * u, 2e-2, "swiglu")
-    wd = (torch.randn(hidden, inter, device=cuda_device) / 40).bfloat16()  # K > one 1024-column chunk
+    wd = (torch.randn(hidden, inter, device=cuda_device) / 40).bfloat16()  # long K: many split-K units
     h = torch.randn(M, inter, device=cuda_device).bfloat16()
     assert_close(G.infer_linear(h, wd), h.float() @ wd.float().T, 1e-2, "long K")
