@@ -708,7 +708,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) attn_bwd_kernel(const BwdParam
 
 // dq = RoPE^T(dq_acc) -> d(q) slice; zero dq/dk/dv slices of padding tokens.
 __global__ void attn_bwd_post_kernel(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, const int* positions,
-                                     const float* cos_tab, const float* sin_tab, int T, int H, const int* sched) {
+                                     const float* cos_tab, const float* sin_tab, int rope_rows, int* err, int T, int H,
+                                     const int* sched) {
   // 16 threads per (token, head) row, 4 rotation pairs (d, d + 64) each: 16-byte fp32 loads,
   // 8-byte bf16 stores, no 64-bit division per element
   const int total = sched[2];
@@ -733,7 +734,8 @@ __global__ void attn_bwd_post_kernel(const float* dq_acc, __nv_bfloat16* dqkv, l
     const float* src = dq_acc + (long)tok * (H * D) + head * D;
     const float4 a = *reinterpret_cast<const float4*>(src + d);
     const float4 b = *reinterpret_cast<const float4*>(src + d + 64);
-    const int pos = positions[tok];
+    int pos = positions[tok];
+    if (!HRM_BOUNDS_OK(pos >= 0 && pos < rope_rows, err, 104)) pos = 0;
     const float4 c = *reinterpret_cast<const float4*>(cos_tab + (long)pos * 64 + d);
     const float4 sn = *reinterpret_cast<const float4*>(sin_tab + (long)pos * 64 + d);
     *reinterpret_cast<uint2*>(q_row + d) = make_uint2(pack_bf16x2(a.x * c.x + b.x * sn.x, a.y * c.y + b.y * sn.y),
@@ -835,7 +837,8 @@ void attn_bwd(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, const a
   attn::attn_bwd_kernel<<<sm_count(), attn::BWD_THREADS, attn::BWD_SMEM, stream>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   attn::attn_bwd_post_kernel<<<1024, 256, 0, stream>>>(p.dq_acc, p.dqkv, p.ld_dqkv, p.positions, p.cos_tab,
-                                                        p.sin_tab, T, (int)H, p.sched);
+                                                        p.sin_tab, (int)cos_tab.size(0),
+                                                        device_error_word().data_ptr<int>(), T, (int)H, p.sched);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -161,12 +161,17 @@ __device__ __forceinline__ void tring_init(TileRing* r, int consumers) {
     mbar_init(&r->empty[i], consumers);
   }
 }
+// A work tile {doc_start, len, prefix, first row} must lie inside the T packed tokens.
+__device__ __forceinline__ bool tile_in_bounds(const int4& t, int T) {
+  return t.x >= 0 && t.y > 0 && t.x + t.y <= T && t.w >= 0 && t.w < t.y && t.z >= 0 && t.z <= t.y;
+}
 __device__ __forceinline__ bool tring_push(TileRing* r, int k, int* counter, const int4* tiles, int H, int n_items,
-                                           int& item, int4& tile) {
+                                           int T, int* err, int& item, int4& tile) {
   const int s = k % kItemRing;
   if (!mbar_wait(&r->empty[s], ((k / kItemRing) & 1) ^ 1)) return false;
   item = atomicAdd(counter, 1);
   tile = item < n_items ? tiles[item / H] : make_int4(0, 0, 0, 0);
+  if (item < n_items && !HRM_BOUNDS_OK(tile_in_bounds(tile, T), err, 100)) item = n_items;  // every role stops
   *reinterpret_cast<volatile int*>(&r->item[s]) = item;
   r->tile[s] = tile;  // published by the release arrive below (the asm clobbers memory)
   mbar_arrive(&r->full[s]);
@@ -258,7 +263,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int kk = 0; ok; ++kk, ++n) {
         int item;
         int4 t;
-        if (!tring_push(&bar->ring, kk, const_cast<int*>(p.sched) + 4, tiles, p.H, n_items, item, t)) { report_error(p.err, kErrAttnWaitTimeout, 10); ok = false; break; }
+        if (!tring_push(&bar->ring, kk, const_cast<int*>(p.sched) + 4, tiles, p.H, n_items, p.T, p.err, item, t)) { report_error(p.err, kErrAttnWaitTimeout, 10); ok = false; break; }
         if (item >= n_items) break;
         const int head = item % p.H;
         const int qx = (p.H + head) * D, kx = (2 * p.H + head) * D, vx = (3 * p.H + head) * D;
@@ -610,6 +615,7 @@ struct BwdParams {
   int cap;
   int* err;
   int profile;  // nonzero: accumulate per-phase clock counts into g_bwd_phase
+  int rope_rows;  // rows of the cos / sin tables
 };
 
 // Phase tracing of the backward (off unless enabled from the host): cycles each role spends
@@ -732,6 +738,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         if (!ring_push(&bar->ring, kk, const_cast<int*>(p.sched) + 6, item)) { report_error(p.err, kErrAttnWaitTimeout, 40); ok = false; break; }
         if (item >= n_items) break;
         const int4 t = tiles[item / p.H];
+        if (!HRM_BOUNDS_OK(tile_in_bounds(t, p.T), p.err, 101)) { ok = false; break; }
         const int head = item % p.H;
         const int qx = (p.H + head) * D, kx = (2 * p.H + head) * D, vx = (3 * p.H + head) * D;
         // K / V of this item can only land once the previous item's UMMAs are done with the
@@ -826,6 +833,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         if (item == INT_MAX) { report_error(p.err, kErrAttnWaitTimeout, 9); ok = false; break; }
         if (item >= n_items) break;
         const int4 t = tiles[item / p.H];
+        if (!HRM_BOUNDS_OK(tile_in_bounds(t, p.T), p.err, 102)) { ok = false; break; }
         const int nqb = bwd_nqb(t);
         pc.mark(13);
         if (!wait_ok(&bar->kv_full, n & 1, 51)) break;
@@ -910,12 +918,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (item == INT_MAX) { report_error(p.err, kErrAttnWaitTimeout, 8); ok = false; break; }
       if (item >= n_items) break;
       const int4 t = tiles[item / p.H];
+      if (!HRM_BOUNDS_OK(tile_in_bounds(t, p.T), p.err, 103)) { ok = false; break; }
       const int head = item % p.H;
       const int doc_start = t.x, len = t.y, prefix = t.z, k0 = t.w;
       const int qs = bwd_qstart(t), nqb = bwd_nqb(t);
       const int key = k0 + row;
       const bool key_ok = key < len;
-      const int pos_k = key_ok ? p.positions[(long)doc_start + key] : 0;  // for the dK RoPE backward
+      int pos_k = key_ok ? p.positions[(long)doc_start + key] : 0;  // for the dK RoPE backward
+      if (!HRM_BOUNDS_OK(pos_k >= 0 && pos_k < p.rope_rows, p.err, 105)) pos_k = 0;
       if (key_ok) {  // the rows are read at the end of the key block: have them in L2 by then
         asm volatile("prefetch.global.L2 [%0];" ::"l"(p.cos_tab + (long)pos_k * 64 + g * 32));
         asm volatile("prefetch.global.L2 [%0];" ::"l"(p.sin_tab + (long)pos_k * 64 + g * 32));
@@ -1163,7 +1173,8 @@ __global__ void attn_bwd_pre_kernel(const __nv_bfloat16* dy, const __nv_bfloat16
                                     const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* d_out,
                                     __nv_bfloat16* dqkv, long ld_dqkv, float* dsum, float* dq_acc, int T, int H);
 __global__ void attn_bwd_post_kernel(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, const int* positions,
-                                     const float* cos_tab, const float* sin_tab, int T, int H, const int* sched);
+                                     const float* cos_tab, const float* sin_tab, int rope_rows, int* err, int T, int H,
+                                     const int* sched);
 }  // namespace attn
 
 static CUtensorMap make_map_rows(const at::Tensor& t, uint32_t box_rows) {
@@ -1239,6 +1250,7 @@ void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
   p.dq_acc = dq_acc.data_ptr<float>();
   p.positions = positions.data_ptr<int>();
   p.cos_tab = cos_tab.data_ptr<float>();
+  p.rope_rows = (int)cos_tab.size(0);
   p.sin_tab = sin_tab.data_ptr<float>();
   p.T = T;
   p.H = (int)H;
@@ -1254,8 +1266,8 @@ void attn_bwd_tc(const at::Tensor& qkv, int64_t H, const at::Tensor& sched, cons
   attn_tc::attn_bwd_tc_kernel<<<sms, attn_tc::BWD_THREADS, attn_tc::BWD_SMEM_BYTES, stream>>>(m_kv, m_q, m_do, m_dq,
                                                                                                p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  attn::attn_bwd_post_kernel<<<1024, 256, 0, stream>>>(p.dq_acc, p.dqkv, p.ld_dqkv, p.positions, p.cos_tab, p.sin_tab, T,
-                                                       (int)H, p.sched);
+  attn::attn_bwd_post_kernel<<<1024, 256, 0, stream>>>(p.dq_acc, p.dqkv, p.ld_dqkv, p.positions, p.cos_tab, p.sin_tab,
+                                                       (int)cos_tab.size(0), p.err, T, (int)H, p.sched);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

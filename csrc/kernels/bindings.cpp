@@ -62,6 +62,7 @@ void adam_atan2(const at::Tensor& p, const at::Tensor& g, const c10::optional<at
                 double beta1, double beta2, double wd, double ema_decay);
 void cast_f32_bf16(const at::Tensor& src, const at::Tensor& dst);
 at::Tensor device_error_word();
+bool debug_bounds_build();
 }  // namespace hrm
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -94,4 +95,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adam_atan2", &hrm::adam_atan2);
   m.def("cast_f32_bf16", &hrm::cast_f32_bf16);
   m.def("device_error_word", &hrm::device_error_word);
+  m.def("debug_bounds_build", &hrm::debug_bounds_build, "built with HRM_DEBUG_BOUNDS (device bounds checks)");
 }

@@ -43,6 +43,23 @@ __device__ __forceinline__ void report_error(int* err, int code, int where) {
 }
 
 // ---------------------------------------------------------------------------------------
+// bounds-check build (HRM_DEBUG_BOUNDS): compute-sanitizer is not available, so a debug build
+// checks tile indices against the packing, stage and TMEM column indices against their
+// ranges, and gather / scatter indices against their tensors. A failed check records
+// (kErrBounds, site, block, thread) in the device error word and the access is skipped; a
+// pipeline that loses a stage that way runs into a bounded wait and winds down. In the
+// regular build every check is the constant `true` and compiles away.
+// ---------------------------------------------------------------------------------------
+#ifdef HRM_DEBUG_BOUNDS
+#define HRM_BOUNDS_OK(cond, err, site) \
+  ((cond) ? true : (::hrm::report_error((err), ::hrm::kErrBounds, (site)), false))
+constexpr bool kDebugBounds = true;
+#else
+#define HRM_BOUNDS_OK(cond, err, site) true
+constexpr bool kDebugBounds = false;
+#endif
+
+// ---------------------------------------------------------------------------------------
 // shared memory / mbarrier
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -19,6 +19,7 @@
 #include "device_setup.h"
 
 namespace hrm {
+at::Tensor device_error_word();
 namespace {
 
 constexpr int D = 128;
@@ -34,7 +35,8 @@ __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
 __global__ void __launch_bounds__(WARPS * 32)
     decode_split_kernel(const __nv_bfloat16* __restrict__ q, long q_sb, long q_sh, const __nv_bfloat16* __restrict__ kc,
                         const __nv_bfloat16* __restrict__ vc, long c_sb, long c_ss, long c_sh,
-                        const int* __restrict__ total, int total_offset, int H, int chunk, float scale_log2,
+                        const int* __restrict__ total, int total_offset, int S_max, int* err, int H, int chunk,
+                        float scale_log2,
                         const __nv_bfloat16* __restrict__ gate, long g_sb, long g_sh,
                         __nv_bfloat16* __restrict__ out, long o_sb, long o_sh, float* __restrict__ part) {
   __shared__ float sm[WARPS], sl[WARPS];
@@ -42,7 +44,8 @@ __global__ void __launch_bounds__(WARPS * 32)
   const int split = blockIdx.x, splits = gridDim.x;
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = total[b] + total_offset;
+  int n = total[b] + total_offset;
+  if (!HRM_BOUNDS_OK(n >= 0 && n <= S_max, err, 90)) n = max(0, min(n, S_max));
   const int c0 = split * chunk, c1 = min(n, c0 + chunk);
 
   float qv[4];
@@ -145,9 +148,10 @@ __global__ void decode_combine_kernel(const float* __restrict__ part, int splits
 // the caches at position lengths[b]: one CTA per sequence, 16-byte copies.
 __global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ gqkv, long ld, int H, const int* __restrict__ lengths,
                                  __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, long c_sb, long c_ss,
-                                 long c_sh) {
+                                 long c_sh, int S_max, int* err) {
   const int b = blockIdx.x;
   const long pos = lengths[b];
+  if (!HRM_BOUNDS_OK(pos >= 0 && pos < S_max, err, 91)) return;
   for (int i = threadIdx.x; i < H * 16; i += blockDim.x) {
     const int h = i >> 4, c = (i & 15) * 8;
     const uint4 k = *reinterpret_cast<const uint4*>(gqkv + b * ld + (long)(2 * H + h) * D + c);
@@ -195,7 +199,8 @@ at::Tensor decode_attention(const at::Tensor& q, const at::Tensor& k_cache, cons
   decode_split_kernel<<<dim3(splits, B * H), WARPS * 32, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), q.stride(1),
       reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()),
-      k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), total.data_ptr<int>(), 0, H, chunk, scale_log2,
+      k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), total.data_ptr<int>(), 0, S,
+      device_error_word().data_ptr<int>(), H, chunk, scale_log2,
       nullptr, 0, 0, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), out.stride(1),
       splits > 1 ? part.data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -230,7 +235,7 @@ at::Tensor decode_attention_gqkv(const at::Tensor& gqkv, int64_t H, const at::Te
   auto vc = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
   const auto* g = reinterpret_cast<const __nv_bfloat16*>(gqkv.data_ptr());
   kv_append_kernel<<<B, 256, 0, stream>>>(g, ld, h, lengths.data_ptr<int>(), kc, vc, k_cache.stride(0),
-                                          k_cache.stride(1), k_cache.stride(2));
+                                          k_cache.stride(1), k_cache.stride(2), S, device_error_word().data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   auto out = at::empty({B, h * D}, gqkv.options());
   const int splits = decode_splits(B, h, S);
@@ -241,7 +246,8 @@ at::Tensor decode_attention_gqkv(const at::Tensor& gqkv, int64_t H, const at::Te
   auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   decode_split_kernel<<<dim3(splits, B * h), WARPS * 32, 0, stream>>>(
       g + (long)h * D, ld, D, kc, vc, k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
-      lengths.data_ptr<int>(), 1, h, chunk, scale_log2, g, ld, D, o, out.stride(0), D,
+      lengths.data_ptr<int>(), 1, S, device_error_word().data_ptr<int>(), h, chunk, scale_log2, g, ld, D, o,
+      out.stride(0), D,
       splits > 1 ? part.data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (splits > 1) {

@@ -91,6 +91,7 @@ struct GemmArgs {
   const float* cos_tab;
   const float* sin_tab;
   int rope_begin, rope_end;
+  int rope_rows;  // rows of the cos / sin tables (positions must be below it)
   // SwiGLU: offset of the "up" half (rows of B in fwd, columns of gate|up in bwd)
   int pair_offset;
   // cross-entropy partials, [n_tiles, M]
@@ -522,7 +523,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // re-read per head from L1) so the live registers stay under the 320-thread cap.
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
         const int c = half;
-        const int pos = row_ok ? args.positions[m] : 0;
+        int pos = row_ok ? args.positions[m] : 0;
+        if (!HRM_BOUNDS_OK(pos >= 0 && pos < args.rope_rows, args.err, 80)) pos = 0;
         const float4* cr = reinterpret_cast<const float4*>(args.cos_tab + (long)pos * 64 + c * 32);
         const float4* sr = reinterpret_cast<const float4*>(args.sin_tab + (long)pos * 64 + c * 32);
 #pragma unroll 1
@@ -947,7 +949,10 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   if (residual) { args.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()); args.ldr = residual->stride(0); }
   if (aux) { args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr()); args.ldaux = aux->stride(0); }
   if (positions) args.positions = positions->data_ptr<int>();
-  if (cos_tab) args.cos_tab = cos_tab->data_ptr<float>();
+  if (cos_tab) {
+    args.cos_tab = cos_tab->data_ptr<float>();
+    args.rope_rows = (int)cos_tab->size(0);
+  }
   if (sin_tab) args.sin_tab = sin_tab->data_ptr<float>();
   args.rope_begin = (int)rope_begin;
   args.rope_end = (int)rope_end;
@@ -1077,7 +1082,10 @@ void gemm_f1(const at::Tensor& x, const at::Tensor& w, int64_t M, int64_t N, int
   args.out = out.data_ptr(); args.ldo = out.stride(0);
   if (out2) { args.out2 = out2->data_ptr(); args.ldo2 = out2->stride(0); }
   if (positions) args.positions = positions->data_ptr<int>();
-  if (cos_tab) args.cos_tab = cos_tab->data_ptr<float>();
+  if (cos_tab) {
+    args.cos_tab = cos_tab->data_ptr<float>();
+    args.rope_rows = (int)cos_tab->size(0);
+  }
   if (sin_tab) args.sin_tab = sin_tab->data_ptr<float>();
   args.rope_begin = (int)rope_begin; args.rope_end = (int)rope_end; args.pair_offset = (int)pair_offset;
   args.err = device_error_word().data_ptr<int>();

@@ -11,6 +11,10 @@
 #include "common.cuh"
 
 namespace hrm {
+at::Tensor device_error_word();
+}  // namespace hrm
+
+namespace hrm {
 
 namespace {
 
@@ -113,11 +117,13 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long ld
 // Embedding: out[t] = bf16(scale * W[id[t]]); grad: gW[id[t]] += scale * dout[t] (fp32).
 // ---------------------------------------------------------------------------------------
 __global__ void embedding_fwd_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ w, long ldw,
-                                     __nv_bfloat16* __restrict__ out, long ldo, int T, int H, float scale) {
+                                     __nv_bfloat16* __restrict__ out, long ldo, int T, int H, float scale, int V,
+                                     int* err) {
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   const long id = ids[row];
+  if (!HRM_BOUNDS_OK(id >= 0 && id < V, err, 95)) return;
   for (int col = lane * 8; col < H; col += 256) {
     float v[8];
     unpack8(*reinterpret_cast<const uint4*>(w + id * ldw + col), v);
@@ -128,11 +134,12 @@ __global__ void embedding_fwd_kernel(const int* __restrict__ ids, const __nv_bfl
 }
 
 __global__ void embedding_bwd_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ dout, long ldo,
-                                     float* __restrict__ gw, long ldg, int T, int H, float scale) {
+                                     float* __restrict__ gw, long ldg, int T, int H, float scale, int V, int* err) {
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   const long id = ids[row];
+  if (!HRM_BOUNDS_OK(id >= 0 && id < V, err, 96)) return;
   for (int col = lane * 8; col < H; col += 256) {
     float v[8];
     unpack8(*reinterpret_cast<const uint4*>(dout + (long)row * ldo + col), v);
@@ -300,7 +307,8 @@ void embedding_fwd(const at::Tensor& ids, const at::Tensor& w, const at::Tensor&
   const int T = (int)ids.numel(), H = (int)w.size(1);
   TORCH_CHECK(H % 8 == 0, "embedding width must be a multiple of 8");
   embedding_fwd_kernel<<<(T + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ids.data_ptr<int>(), bf(w), w.stride(0), bfm(out), out.stride(0), T, H, (float)scale);
+      ids.data_ptr<int>(), bf(w), w.stride(0), bfm(out), out.stride(0), T, H, (float)scale, (int)w.size(0),
+      device_error_word().data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -308,7 +316,8 @@ void embedding_bwd(const at::Tensor& ids, const at::Tensor& dout, const at::Tens
   c10::cuda::CUDAGuard guard(dout.device());
   const int T = (int)ids.numel(), H = (int)dout.size(1);
   embedding_bwd_kernel<<<(T + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ids.data_ptr<int>(), bf(dout), dout.stride(0), gw.data_ptr<float>(), gw.stride(0), T, H, (float)scale);
+      ids.data_ptr<int>(), bf(dout), dout.stride(0), gw.data_ptr<float>(), gw.stride(0), T, H, (float)scale,
+      (int)gw.size(0), device_error_word().data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -359,6 +368,9 @@ void cast_f32_bf16(const at::Tensor& src, const at::Tensor& dst) {
 // device error word: 4 x int32 per device, zero until a kernel reports a bounded-wait
 // timeout (code, site, block, thread).
 // ---------------------------------------------------------------------------------------
+// True when the extension was built with HRM_DEBUG_BOUNDS (device-side bounds checks).
+bool debug_bounds_build() { return kDebugBounds; }
+
 at::Tensor device_error_word() {
   static at::Tensor* words = new at::Tensor[16];  // intentionally leaked: no teardown after the driver
   int dev;

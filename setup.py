@@ -3,7 +3,8 @@
     python setup.py build_ext --inplace
 
 * ``hrm_text_b200._C``    — sm_100a CUDA kernels (csrc/kernels), compiled only for
-  ``compute_100a/sm_100a`` with line info.
+  ``compute_100a/sm_100a`` with line info. ``HRM_DEBUG_BOUNDS=1`` builds the bounds-checked
+  variant (``_C.debug_bounds_build()`` reports which one is loaded).
 * ``hrm_text_b200._host`` — host C++ (csrc/host): the multipack LPT allocator.
 """
 import glob
@@ -23,6 +24,10 @@ nvcc_flags = [
     "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
     "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_BFLOAT16_OPERATORS__",
 ]
+
+# HRM_DEBUG_BOUNDS=1: bounds-check build (device-side index checks that record the error word)
+if os.environ.get("HRM_DEBUG_BOUNDS", "0") == "1":
+    nvcc_flags.append("-DHRM_DEBUG_BOUNDS")
 
 cuda_sources = sorted(glob.glob(os.path.join("csrc", "kernels", "*.cu"))) + ["csrc/kernels/bindings.cpp"]
 
