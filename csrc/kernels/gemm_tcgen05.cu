@@ -103,6 +103,7 @@ struct GemmArgs {
   int* err;
   int stream_k;
   int splitk;  // EPI_F32ADD: > 1 selects K-chunk-major split-K instead of stream-K
+  long splitk_slice;  // EPI_F32ADD: 0 = add into out (atomics); else split q stores into out + q * splitk_slice
   // F1: all-gather fused into the first GEMM that reads a sharded weight (B operand)
   const CUtensorMap* f1_peer_maps;  // [world] maps over each rank's bf16 shard of this weight
   int f1_shard_rows;                // rows per rank shard (a multiple of 128)
@@ -505,6 +506,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       } else if constexpr (EPI == EPI_F32ADD) {
         float* out = reinterpret_cast<float*>(args.out);
+        // deterministic split-K: the unit of K chunk q stores its partial into slice q (the
+        // caller sums the slices in order); kb0 = floor(nk * q / split) identifies q
+        const bool sliced = args.splitk_slice != 0;
+        if (sliced) out += (long)((mode == 2) ? (kb0 * split + sched.nk - 1) / sched.nk : 0) * args.splitk_slice;
 #pragma unroll 1
         for (int c = half * 4; c < half * 4 + 4; ++c) {
           float v[32];
@@ -512,9 +517,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int n = nt * BN + c * 32;
           if (row_ok && n < args.N) {
             float4* dst = reinterpret_cast<float4*>(out + (long)m * args.ldo + n);
+            if (sliced) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              atomicAdd(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+              for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            } else {
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                atomicAdd(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+            }
           }
         }
       } else if constexpr (EPI == EPI_ROPE) {
@@ -940,6 +950,15 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   if (epi == EPI_CE && out.numel() == 0) {  // cross-entropy statistics without storing the logits
     args.out = nullptr;
     args.ldo = 0;
+  } else if (epi == EPI_F32ADD && out.dim() == 3) {  // deterministic split-K: [split, M, N] fp32 slices
+    TORCH_CHECK(out.stride(2) == 1 && out.stride(1) % 4 == 0 && out.size(1) == M && out.size(2) == N &&
+                    out.size(0) >= 1 && out.size(0) <= (K + BK - 1) / BK,
+                "gemm: split-K slices must be [split <= k-blocks, M, N] fp32 with 16-byte aligned rows");
+    args.out = out.data_ptr();
+    args.ldo = out.stride(1);
+    args.splitk_slice = out.stride(0);
+    splitk = out.size(0);
+    stream_k = splitk > 1;  // one slice: whole tiles, plain stores
   } else {
     args.out = out.data_ptr();
     args.ldo = out.stride(0);

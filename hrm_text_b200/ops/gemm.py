@@ -137,8 +137,8 @@ def lm_head_ce_dlogits(x: Tensor, w_chunk: Tensor, labels: Tensor, lse: Tensor, 
 
 # ---------------------------------------------------------------------------------------
 # inference: the same layers for any M; decode steps (M <= 128) run the tcgen05 GEMM in
-# split-K mode (K spread over all SMs, fp32 partials added into a zeroed [M, N] buffer) and a
-# finishing kernel with the epilogue (csrc/kernels/skinny_gemm.cu)
+# split-K mode (K spread over all SMs, one fp32 [M, N] slice per K range) and a finishing
+# kernel that sums the slices in order and applies the epilogue (csrc/kernels/skinny_gemm.cu)
 # ---------------------------------------------------------------------------------------
 DECODE_MAX_M = 128
 _SM_COUNT: dict = {}
@@ -153,7 +153,7 @@ def _decode_gemm(x: Tensor, w: Tensor) -> Tensor:
         sms = _SM_COUNT[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
     tiles = -(-N // 256)
     split = max(1, min(-(-K // 64), round(2 * sms / tiles)))
-    acc = torch.zeros((M, N), dtype=torch.float32, device=dev)
+    acc = torch.empty((split, M, N), dtype=torch.float32, device=dev)  # every element is written
     _gemm(x, False, w, False, M, N, K, EPI_F32ADD, acc, stream_k=True, splitk=split)
     return acc
 
