@@ -233,9 +233,11 @@ def run_ours(args):
             "config": {"model": f"HRM-Text {args.size}", "global_batch": global_batch, "seq_len": MAX_SEQ_LEN,
                        "tokens_per_gpu": tokens_per_gpu, "bp_steps": bp, "parallelism": f"dp{world}",
                        "sharding": "in-house dim-0 param/optimizer sharding; " + (
-                           "block weights: all-gather fused into the QKV/gate-up GEMMs (F1), wgrad + reduce-scatter + "
-                           "AdamATan2 in one kernel (F2) over NVLink peer memory; embedding/head over NCCL"
-                           if fused else "NCCL reduce-scatter / all-gather"),
+                           "block weights: all-gather inside the first GEMM of the step reading each weight (F1), "
+                           "reduce-scatter pushed from the last wgrad GEMM's epilogue over NVLink peer memory (F2) "
+                           "+ one step-end inbox-sum/AdamATan2 kernel; embedding/head/norms over NCCL"
+                           if fused else "NCCL reduce-scatter / all-gather" if world > 1 else "single GPU"),
+                       "collective": ("fused F1/F2" if fused else "NCCL") if world > 1 else "none",
                        "l2": "inputs larger than L2 (per-step working set >> 126 MB)"},
             "clocks": clock_info, "e2e": e2e, "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
             "impl": "ours", "final_loss": last_loss, "peak_memory_gb": round(peak_gb, 2),

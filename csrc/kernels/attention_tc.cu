@@ -580,24 +580,32 @@ __global__ void zero_tail_kernel(__nv_bfloat16* out, __nv_bfloat16* y, long ld_o
 // so the softmax of b+1 overlaps the tensor-core work of b (two TMEM regions).
 // Warp roles (320 threads): 0 TMA, 1 UMMA, 2..9 compute. Compute warp group g (warps 2-5,
 // 6-9) owns queries [32g, 32g+32) of every block: the softmax of that half (two warps per
-// scheduler), then, after the next block's softmax, that half of dQ^T, which it moves from TMEM
-// through a warp-private shared-memory tile into the fp32 dQ accumulator with one tensor
-// reduction per warp and block (cp.reduce.async.bulk.tensor .add, a [32 x 32] fp32 box)
-// instead of one atomic per element. At the end of the key block group 0 applies
-// the RoPE backward to dK and writes it, group 1 writes dV.
+// scheduler), then, after writing the next block's P^T / dS^T, that half of dQ^T, which it
+// moves from TMEM through a warp-private shared-memory box into the fp32 dQ accumulator with
+// one tensor reduction per warp and block (cp.reduce.async.bulk.tensor .add, [32 x 32] fp32).
+// P^T / dS^T tiles are double-buffered by block parity, so a block's softmax only waits for
+// the UMMAs of the block two back; the dQ boxes of a block are staged in that block's consumed
+// P^T / dS^T pair. At the end of the key block group 0 applies the RoPE backward to dK and
+// writes it, group 1 writes dV.
 // TMEM: S^T_0 [0,64), dP^T_0 [64,128), S^T_1 [128,192), dP^T_1 [192,256), dV [256,384),
 // dK [384,512).
-// Shared: K 32 KB, V 32 KB, Q 2x16 KB, dO 2x16 KB, P^T 16 KB, dS^T 16 KB, lse/D 2 KB,
-// dQ staging 8 x 4 KB.
+// Shared: K 32 KB, V 32 KB, Q 3x16 KB, dO 3x16 KB, 2 x (P^T 16 KB | dS^T 16 KB), lse/D 2 KB.
 // =======================================================================================
 constexpr int BWD_THREADS = 320;
 constexpr int BQB = 64;                 // queries per block
 constexpr int QTILE_BYTES = BQB * 128 * 2;   // [64][128] bf16 = two [64][64] boxes (16 KB)
 constexpr int PTILE_BYTES = 128 * BQB * 2;   // [128 keys][64 queries] bf16 (16 KB)
 constexpr int QSTAGES = 3;                   // Q / dO ring depth
-constexpr int DQ_STAGE_BYTES = 32 * 32 * 4;  // per compute warp: [32 queries][32 dims] fp32
-static_assert(8 * DQ_STAGE_BYTES == 2 * PTILE_BYTES, "dQ staging aliases the P^T / dS^T tiles");
-constexpr int BWD_SMEM_BYTES = 1024 + 2 * TILE_BYTES + 2 * QSTAGES * QTILE_BYTES + 2 * PTILE_BYTES + 2048 + 512;
+// P^T | dS^T pairs are double-buffered by block parity, so the softmax of block b waits only for
+// the UMMAs of block b - 2. A drained block's dQ^T is staged (per compute warp [32 queries][32
+// dims] fp32) in that block's own, consumed, P^T | dS^T pair.
+constexpr int PD_BYTES = 2 * PTILE_BYTES;
+constexpr int DQ_STAGE_BYTES = 32 * 32 * 4;
+static_assert(8 * DQ_STAGE_BYTES == PD_BYTES, "dQ staging aliases one P^T | dS^T pair");
+// No alignment slack: with no static shared memory the dynamic window starts 1024-byte aligned
+// (the kernel checks, and reports an error instead of running misaligned).
+constexpr int BWD_SMEM_BYTES = 2 * TILE_BYTES + 2 * QSTAGES * QTILE_BYTES + 2 * PD_BYTES + 2048 + 512;
+static_assert(BWD_SMEM_BYTES <= 232448, "backward exceeds the shared-memory limit");
 constexpr uint32_t TB_S = 0, TB_DP = 64, TB_REGION = 128, TB_DV = 256, TB_DK = 384;
 
 struct BwdParams {
@@ -651,9 +659,10 @@ struct BwdBarriers {
   uint64_t kv_full, kv_done, kv_free;
   uint64_t qd_full[QSTAGES], qd_empty[QSTAGES];
   uint64_t s_full[2], dq_full[2], dq_free[2];
-  uint64_t p_full, p_free, stage_free, drain;
+  uint64_t p_full[2], p_free[2], stage_free[2], drain;
   ItemRing ring;
 };
+static_assert(sizeof(BwdBarriers) + sizeof(uint32_t) <= 512, "backward barriers exceed their shared-memory slot");
 
 // smem box -> global, element-wise fp32 add, through a tensor map (one instruction per box)
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
@@ -673,19 +682,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_dq,
                        const BwdParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0u) {  // the swizzled tiles need 1024-byte alignment
+    if (threadIdx.x == 0) report_error(p.err, kErrAttnWaitTimeout, 65);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sK = smem;
   uint8_t* sV = sK + TILE_BYTES;
   uint8_t* sQ = sV + TILE_BYTES;               // QSTAGES stages
   uint8_t* sDO = sQ + QSTAGES * QTILE_BYTES;   // QSTAGES stages
-  uint8_t* sP = sDO + QSTAGES * QTILE_BYTES;
-  uint8_t* sDS = sP + PTILE_BYTES;
-  float* sLse = reinterpret_cast<float*>(sDS + PTILE_BYTES);  // per compute warp: [32] lse, [32] D
-  // dQ staging, per compute warp [32][32] fp32, aliases the P^T / dS^T tiles: a block's dQ^T
-  // is drained after the UMMAs that read its P^T / dS^T completed, before the next block's
-  // P^T / dS^T are written
-  float* sDQ = reinterpret_cast<float*>(sP);
+  uint8_t* sPD = sDO + QSTAGES * QTILE_BYTES;  // 2 x (P^T [16 KB] | dS^T [16 KB]), block parity
+  float* sLse = reinterpret_cast<float*>(sPD + 2 * PD_BYTES);  // per compute warp: [32] lse, [32] D
   BwdBarriers* bar = reinterpret_cast<BwdBarriers*>(sLse + 512);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
 
@@ -706,9 +714,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&bar->dq_full[s], 1);
       mbar_init(&bar->dq_free[s], 256);
     }
-    mbar_init(&bar->p_full, 256);
-    mbar_init(&bar->p_free, 1);
-    mbar_init(&bar->stage_free, 8);  // lane 0 of each compute warp
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->p_full[s], 256);
+      mbar_init(&bar->p_free[s], 1);
+      mbar_init(&bar->stage_free[s], 8);  // lane 0 of each compute warp
+    }
     mbar_init(&bar->drain, 1);
     ring_init(&bar->ring, 9);  // UMMA thread + 8 compute warps
     fence_mbar_init();
@@ -731,7 +741,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     // ---------------------------------------------------------------- TMA loads
     if (lane == 0) {
       int n = 0, qb_all = 0;
-      int last_kv = -1, last_q[QSTAGES] = {-1, -1, -1};
+      int last_kv = -1, last_q[QSTAGES];
+#pragma unroll
+      for (int s = 0; s < QSTAGES; ++s) last_q[s] = -1;
       bool ok = true;
       for (int kk = 0; ok; ++kk, ++n) {
         int item;
@@ -790,7 +802,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       constexpr uint32_t id_kv = umma_idesc_bf16(128, 128, 0, 1);  // dV, dK
       constexpr uint32_t id_dq = umma_idesc_bf16(128, 64, 1, 1);   // dQ^T
       const uint32_t kb = smem_u32(sK), vb = smem_u32(sV), qb0 = smem_u32(sQ), db0 = smem_u32(sDO);
-      const uint32_t pb = smem_u32(sP), dsb = smem_u32(sDS);
+      const uint32_t pb = smem_u32(sPD), dsb = pb + PTILE_BYTES;
       int n = 0, b = 0;
       bool ok = true;
       PhaseClock pc(p.profile != 0);
@@ -804,8 +816,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       auto finish = [&](int bb, bool first) -> bool {
         const int s = bb & 1, qst = bb % QSTAGES;
         const uint32_t qs = qb0 + qst * QTILE_BYTES, ds = db0 + qst * QTILE_BYTES;
+        const uint32_t pbb = pb + s * PD_BYTES, dsbb = dsb + s * PD_BYTES;  // block parity buffers
         pc.mark(13);
-        if (!wait_ok(&bar->p_full, bb & 1, 54)) return false;
+        if (!wait_ok(&bar->p_full[s], (bb >> 1) & 1, 54)) return false;
         pc.mark(11);
         if (first && !wait_ok(&bar->kv_free, (n & 1) ^ 1, 55)) return false;
         pc.mark(12);
@@ -815,16 +828,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           const uint64_t bo = umma_desc_sw128(ds + k * 2048, QTILE_BYTES / 2, 1024);
           const uint64_t bq = umma_desc_sw128(qs + k * 2048, QTILE_BYTES / 2, 1024);
           const uint32_t acc = (!first || k > 0) ? 1u : 0u;
-          umma_f16_ss(tmem + TB_DV, umma_desc_sw128(pb + k * 32, 16, 1024), bo, id_kv, acc);
-          umma_f16_ss(tmem + TB_DK, umma_desc_sw128(dsb + k * 32, 16, 1024), bq, id_kv, acc);
+          umma_f16_ss(tmem + TB_DV, umma_desc_sw128(pbb + k * 32, 16, 1024), bo, id_kv, acc);
+          umma_f16_ss(tmem + TB_DK, umma_desc_sw128(dsbb + k * 32, 16, 1024), bq, id_kv, acc);
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {  // 16 keys per step
           umma_f16_ss(tmem + s * TB_REGION + TB_S, umma_desc_sw128(kb + k * 2048, TILE_BYTES / 2, 1024),
-                      umma_desc_sw128(dsb + k * 2048, PTILE_BYTES, 1024), id_dq, k > 0);
+                      umma_desc_sw128(dsbb + k * 2048, PTILE_BYTES, 1024), id_dq, k > 0);
         }
         umma_commit(&bar->qd_empty[qst]);
-        umma_commit(&bar->p_free);
+        umma_commit(&bar->p_free[s]);
         umma_commit(&bar->dq_full[s]);
         return true;
       };
@@ -883,7 +896,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const uint32_t lo = (uint32_t)(quarter * 32) << 16;
     float* lse_b = sLse + (warp - 2) * 64;  // warp-private copy of this block's lse / D
     float* d_b = lse_b + 32;
-    float* stage = sDQ + (warp - 2) * (32 * 32);  // dQ staging [32 queries][32 dims]
     int n = 0, b = 0;
     bool ok = true;
     PhaseClock pc(p.profile != 0 && warp == 2);
@@ -899,16 +911,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&bar->dq_free[sreg]);  // TMEM region reusable: dQ^T is in registers
-      if (lane == 0) bulk_wait_group_read0();  // the previous reduction has read the stage
-      __syncwarp();
+      // staging: this warp's 4 KB of block bb's P^T | dS^T pair, which its UMMAs (complete, see
+      // dq_full) no longer read; no warp writes P^T(bb + 2) there before every warp's reduction
+      // of this box has read it (stage_free[bb & 1])
+      float* stage = reinterpret_cast<float*>(sPD + sreg * PD_BYTES) + (warp - 2) * (32 * 32);
 #pragma unroll
       for (int e = 0; e < 32; ++e) stage[e * 32 + lane] = __uint_as_float(r[e]);
       fence_async_smem();
       __syncwarp();
       // one [32 queries][32 dims] fp32 box added into dQ; rows past the document receive the
       // exact zeros of their masked dS (rows past T are clipped by the tensor map)
-      if (lane == 0) tma_reduce_add_2d(&tm_dq, stage, head * D + quarter * 32, t.x + qbase + g * 32);
-      if (lane == 0) bulk_commit_group();
+      if (lane == 0) {
+        tma_reduce_add_2d(&tm_dq, stage, head * D + quarter * 32, t.x + qbase + g * 32);
+        bulk_commit_group();
+      }
       pc.mark(5);
       return true;
     };
@@ -995,19 +1011,19 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           }
         }
         pc.mark(1);
-        if (!warp_wait(&bar->p_free, (b & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 62); ok = false; break; }
-        pc.mark(2);
-        // the P^T / dS^T tiles of block b - 1 are consumed: drain dQ^T(b - 1) through them
-        if (qb > 0 && !drain_dq(b - 1, t, head, qbase - BQB)) { ok = false; break; }
-        // every compute warp's reduction has read its staging box before P^T / dS^T(b) land
-        if (lane == 0) {
-          bulk_wait_group_read0();
-          mbar_arrive(&bar->stage_free);
+        // pair b & 1 was last read by the UMMAs of block b - 2 ...
+        if (!warp_wait(&bar->p_free[b & 1], ((b >> 1) & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 62); ok = false; break; }
+        // ... and staged dQ^T(b - 2) for every warp's reduction
+        if (b >= 2) {
+          if (lane == 0) {
+            bulk_wait_group_read0();  // this warp's reduction of dQ^T(b - 2), its latest, has read its box
+            mbar_arrive(&bar->stage_free[b & 1]);
+          }
+          if (!warp_wait(&bar->stage_free[b & 1], ((b - 2) >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 64); ok = false; break; }
         }
-        if (!warp_wait(&bar->stage_free, b & 1)) { report_error(p.err, kErrAttnWaitTimeout, 64); ok = false; break; }
-        pc.mark(7);
-        uint8_t* prow = sP + row * 128;
-        uint8_t* drow = sDS + row * 128;
+        pc.mark(2);
+        uint8_t* prow = sPD + (b & 1) * PD_BYTES + row * 128;
+        uint8_t* drow = prow + PTILE_BYTES;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {  // 16-byte pieces g*4 + i of the 128-byte swizzled row
           const int off = ((g * 4 + i) ^ (row & 7)) << 4;
@@ -1016,8 +1032,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         }
         fence_async_smem();
         tc_fence_before();
-        mbar_arrive(&bar->p_full);
+        mbar_arrive(&bar->p_full[b & 1]);
         pc.mark(3);
+        // dQ^T of block b - 1, whose UMMAs ran while this block's softmax did
+        if (qb > 0 && !drain_dq(b - 1, t, head, qbase - BQB)) { ok = false; break; }
       }
       if (!ok) break;
       if (!drain_dq(b - 1, t, head, qs + (nqb - 1) * BQB)) { ok = false; break; }

@@ -9,17 +9,12 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
           const c10::optional<at::Tensor>& sin_tab, int64_t rope_begin, int64_t rope_end, int64_t pair_offset,
           const c10::optional<at::Tensor>& labels, const c10::optional<at::Tensor>& ce_max,
           const c10::optional<at::Tensor>& ce_sum, const c10::optional<at::Tensor>& ce_arg,
-          const c10::optional<at::Tensor>& ce_tgt, bool stream_k, int64_t splitk);
-at::Tensor encode_shard_maps(const std::vector<int64_t>& shard_addrs, int64_t shard_rows, int64_t cols);
-void gemm_f1(const at::Tensor& x, const at::Tensor& w, int64_t M, int64_t N, int64_t K, int64_t epi,
-             const at::Tensor& out, const c10::optional<at::Tensor>& out2, const c10::optional<at::Tensor>& positions,
-             const c10::optional<at::Tensor>& cos_tab, const c10::optional<at::Tensor>& sin_tab, int64_t rope_begin,
-             int64_t rope_end, int64_t pair_offset, const at::Tensor& peer_maps, int64_t shard_rows,
-             const at::Tensor& flags);
-void gemm_f2(const at::Tensor& dy, const at::Tensor& x, int64_t M, int64_t N, int64_t K, const at::Tensor& local_grad,
-             const at::Tensor& base32, const at::Tensor& base16, const std::vector<int64_t>& offsets,
-             int64_t shard_rows, int64_t inbox_stride, int64_t rank, int64_t world, const at::Tensor& hyper,
-             double beta1, double beta2, double wd, double ema_decay, bool has_m, bool has_ema);
+          const c10::optional<at::Tensor>& ce_tgt, bool stream_k, int64_t splitk,
+          const c10::optional<at::Tensor>& jobs);
+void copy_jobs(const at::Tensor& jobs, int64_t device);
+void shard_update(const at::Tensor& items, const at::Tensor& buf, const std::vector<int64_t>& offs,
+                  const at::Tensor& full_grad, const at::Tensor& shard16, const at::Tensor& ran, int64_t world,
+                  int64_t rank, const at::Tensor& hyper, double beta1, double beta2, double wd, double ema_decay);
 int64_t attn_schedule_capacity(int64_t T, int64_t n_cu);
 void attn_schedule(const at::Tensor& cu_seqlens, const at::Tensor& prefix_lens, bool causal, int64_t T,
                    const at::Tensor& sched);
@@ -68,9 +63,8 @@ bool debug_bounds_build();
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "HRM-Text sm_100a kernels";
   m.def("gemm", &hrm::gemm, "tcgen05 GEMM with fused epilogues");
-  m.def("encode_shard_maps", &hrm::encode_shard_maps);
-  m.def("gemm_f1", &hrm::gemm_f1, "all-gather fused into the first GEMM reading a sharded weight");
-  m.def("gemm_f2", &hrm::gemm_f2, "weight-gradient GEMM fused with reduce-scatter and AdamATan2");
+  m.def("copy_jobs", &hrm::copy_jobs, "fused-collective copy jobs (gather / push) without a GEMM to ride on");
+  m.def("shard_update", &hrm::shard_update, "step-end inbox reduction + AdamATan2 on this rank's shards");
   m.def("attn_schedule_capacity", &hrm::attn_schedule_capacity);
   m.def("attn_schedule", &hrm::attn_schedule);
   m.def("attn_fwd", &hrm::attn_fwd);

@@ -32,6 +32,25 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   return t;
 }
 
+// One AdamATan2 element update (the reference optimizer's order of operations): decoupled
+// weight decay, second moment, first moment (beta1 > 0), atan2(m, sqrt(v) / sqrt(bc2)) step.
+// hyper = [lr, 1/(1-beta1^t), 1/sqrt(1-beta2^t)]. Returns the new parameter.
+__device__ __forceinline__ float adam_atan2_update(float p, float g, bool has_m, float& m, float& v, float lr,
+                                                   float inv_bc1, float inv_bc2_sqrt, float beta1, float beta2,
+                                                   float wd) {
+  if (wd != 0.f) p *= 1.f - lr * wd;
+  v = beta2 * v + (1.f - beta2) * g * g;
+  const float denom = sqrtf(v) * inv_bc2_sqrt;
+  float upd;
+  if (has_m) {
+    m = m + (1.f - beta1) * (g - m);
+    upd = atan2f(m, denom) * (lr * inv_bc1);
+  } else {
+    upd = atan2f(g, denom) * lr;
+  }
+  return p - upd;
+}
+
 __device__ __forceinline__ void report_error(int* err, int code, int where) {
   if (err != nullptr) {
     if (atomicCAS(err, 0, code) == 0) {

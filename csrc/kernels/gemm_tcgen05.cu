@@ -37,6 +37,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "collective_jobs.cuh"
 #include "common.cuh"
 #include "device_setup.h"
 
@@ -50,7 +51,6 @@ enum GemmEpilogue : int {
   EPI_SWIGLU = 4,
   EPI_SWIGLU_BWD = 5,
   EPI_CE = 6,
-  EPI_F2 = 7,  // fp32 wgrad tile -> owner's inbox over NVLink; owner sums the slots and runs AdamATan2
   EPI_CE_BWD = 8,  // recomputed logits -> (softmax - onehot) * dloss, bf16 (one V chunk of the LM head)
 };
 
@@ -61,20 +61,16 @@ constexpr int EPI_WARPS = 8;
 constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int GEMM_SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256;
-// F2 only: a 32x32 fp32 transpose tile per epilogue warp, so that peer stores and the
-// optimizer's state accesses run as full 128-byte row segments instead of 16-byte pieces.
-constexpr int F2_STAGE_BYTES = EPI_WARPS * 32 * 32 * 4;
 template <int EPI>
-constexpr int gemm_smem_bytes() { return GEMM_SMEM_BYTES + (EPI == 7 ? F2_STAGE_BYTES : 0); }
+constexpr int gemm_smem_bytes() { return GEMM_SMEM_BYTES; }
 // CTA-pair (cta_group::2) variant: a 256 x 256 tile per pair of SMs, each SM stages its 128
 // rows of A and its 128 columns of B, so a k-block costs each SM 32 KB instead of 48 KB of
 // operand traffic for the same tensor-core work; 6 stages fit the same shared memory.
 constexpr int PAIR_STAGES = 6;
 constexpr int PAIR_SMEM_BYTES = 1024 + PAIR_STAGES * (A_STAGE_BYTES + B_STAGE_BYTES / 2) + 256;
-static_assert(PAIR_SMEM_BYTES + F2_STAGE_BYTES <= 232448, "pair GEMM exceeds the shared-memory limit");
+static_assert(PAIR_SMEM_BYTES <= 232448, "pair GEMM exceeds the shared-memory limit");
 template <int EPI>
-constexpr int pair_smem_bytes() { return PAIR_SMEM_BYTES + (EPI == 7 ? F2_STAGE_BYTES : 0); }
-static_assert(GEMM_SMEM_BYTES + F2_STAGE_BYTES <= 232448, "F2 GEMM exceeds the shared-memory limit");
+constexpr int pair_smem_bytes() { return PAIR_SMEM_BYTES; }
 
 struct GemmArgs {
   int M, N, K;
@@ -104,20 +100,8 @@ struct GemmArgs {
   int stream_k;
   int splitk;  // EPI_F32ADD: > 1 selects K-chunk-major split-K instead of stream-K
   long splitk_slice;  // EPI_F32ADD: 0 = add into out (atomics); else split q stores into out + q * splitk_slice
-  // F1: all-gather fused into the first GEMM that reads a sharded weight (B operand)
-  const CUtensorMap* f1_peer_maps;  // [world] maps over each rank's bf16 shard of this weight
-  int f1_shard_rows;                // rows per rank shard (a multiple of 128)
-  int* f1_flags;                    // [n_tiles] 0 = not gathered this step, 1 = local copy written
-  // F2: weight gradient -> reduce-scatter -> AdamATan2 on the owner's shard
-  int f2_split, f2_world, f2_shard_rows, f2_cols;
-  const unsigned long long* f2_base32;  // [world] fp32 symmetric buffer base addresses
-  const unsigned long long* f2_base16;  // [world] bf16 symmetric buffer base addresses
-  long f2_grad_off, f2_master_off, f2_m_off, f2_v_off, f2_ema_off, f2_s16_off, f2_cnt_off;
-  long f2_inbox_stride;  // fp32 elements between source-rank slots of the inbox
-  int f2_rank;
-  const float* f2_hyper;  // [lr, 1/(1-b1^t), 1/sqrt(1-b2^t)]
-  float f2_beta1, f2_beta2, f2_wd, f2_ema;
-  int f2_has_m, f2_has_ema;
+  // fused-collective copy jobs, run by the epilogue warps before their first tile
+  CopyJobs jobs;
 };
 
 struct TileSched {
@@ -241,11 +225,10 @@ __device__ __forceinline__ void tmem_load_f32x32(uint32_t taddr, float (&v)[32])
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-template <int A_MN, int B_MN, int EPI, int F1 = 0, int PAIR = 0>
+template <int A_MN, int B_MN, int EPI, int PAIR = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
-  static_assert(!(PAIR && F1), "the fused all-gather GEMM runs on single CTAs");
   constexpr int kStages = PAIR ? PAIR_STAGES : STAGES;
   constexpr int kBStage = PAIR ? B_STAGE_BYTES / 2 : B_STAGE_BYTES;
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
@@ -317,18 +300,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for_each_segment(sched, mode, split, unit, units, [&](int tile, int kb0, int kb1) -> bool {
         const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
-        // F1: tiles of the first M row read the weight from its owner's shard (peer memory,
-        // plain TMA) and write it through to the local resident copy; other tiles wait for
-        // that copy and read it locally.
-        const bool f1_writer = F1 && mt == 0;
-        if (F1 && !f1_writer) {
-          if (!wait_flag(args.f1_flags + nt, 1)) {
-            report_error(args.err, kErrPeerWaitTimeout, 5);
-            ok = false;
-            return false;
-          }
-          fence_proxy_async_global();
-        }
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages, r = it / kStages;
           if (!mbar_wait(&empty_bar[s], (r & 1) ^ 1)) {
@@ -377,14 +348,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               r0 = nt * BN;
               r1 = nt * BN + 128;
             }
-            if (f1_writer) {
-              const int o0 = r0 / args.f1_shard_rows, o1 = r1 / args.f1_shard_rows;
-              tma_load_2d(b_dst, args.f1_peer_maps + o0, &full_bar[s], kb * BK, r0 - o0 * args.f1_shard_rows);
-              tma_load_2d(b_dst + 16384, args.f1_peer_maps + o1, &full_bar[s], kb * BK, r1 - o1 * args.f1_shard_rows);
-            } else {
-              tma_load_2d(b_dst, &tmB, &full_bar[s], kb * BK, r0);
-              tma_load_2d(b_dst + 16384, &tmB, &full_bar[s], kb * BK, r1);
-            }
+            tma_load_2d(b_dst, &tmB, &full_bar[s], kb * BK, r0);
+            tma_load_2d(b_dst + 16384, &tmB, &full_bar[s], kb * BK, r1);
           } else {
 #pragma unroll
             for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[s], nt * BN + j * 64, kb * BK);
@@ -437,22 +402,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             umma_commit_pair_mc(&empty_bar[s], 3);  // frees this stage in both CTAs
             continue;
           }
-          if (F1 && tile < sched.n_tiles) {  // first M row: write the gathered B boxes through
-            const int nt = tile;
-            const int r0 = (EPI == EPI_SWIGLU) ? nt * 128 : nt * BN;
-            const int r1 = (EPI == EPI_SWIGLU) ? args.pair_offset + nt * 128 : nt * BN + 128;
-            uint8_t* b_src = sB + s * B_STAGE_BYTES;
-            tma_store_2d(&tmB, b_src, kb * BK, r0);
-            tma_store_2d(&tmB, b_src + 16384, kb * BK, r1);
-            bulk_commit();
-            bulk_wait_read0();  // the stage may be refilled only after the store read it
-          }
           umma_commit(&empty_bar[s]);  // frees the smem stage when these UMMAs finish
-        }
-        if (F1 && tile < sched.n_tiles) {
-          bulk_wait0();                // local copy of this weight tile is in global memory
-          fence_proxy_async_global();  // ... and visible to the TMA loads of other CTAs
-          st_release_gpu(args.f1_flags + tile, 1);
         }
         if constexpr (PAIR)
           umma_commit_pair_mc(&tfull_bar[acc], 3);  // both CTAs' accumulator halves ready
@@ -473,6 +423,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;  // which column half of the tile this warp handles
     const int row = quarter * 32 + lane;
+    if (args.jobs.g_src != nullptr || args.jobs.p_src != nullptr)
+      run_copy_jobs(args.jobs, (int)blockIdx.x * EPI_WARPS + (warp - 2), (int)gridDim.x * EPI_WARPS, lane);
     int local = 0;
     for_each_segment(sched, mode, split, unit, units, [&](int tile, int kb0, int kb1) -> bool {
       const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
@@ -628,107 +580,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             store_bf16x32(dgu + (long)m * args.ldo + args.pair_offset + f, u);
           }
         }
-      } else if constexpr (EPI == EPI_F2) {
-        // Tile rows belong to one owner rank. A non-owner stores its complete fp32 partial
-        // (TMEM accumulator + the local gradient of the step's earlier calls) into its slot
-        // of the owner's inbox with plain 16-byte stores and counts itself on the owner, one
-        // system-scope atomic per warp. The owner waits (bounded) for the world-1 peer
-        // counts, adds the peers' slots to its own partial still held in TMEM and applies
-        // AdamATan2 to its master weights / state: all optimizer traffic stays in local HBM
-        // and NVLink carries the fp32 gradient once, as a reduce-scatter would.
-        // Each 32x32 chunk goes through the warp's smem tile (XOR-swizzled float4 slots) so
-        // that every global access covers 4 rows x 128 contiguous bytes per instruction.
-        const int m0 = mt * TILE_M + (int)cta_rank * BM;
-        const int owner = m0 / args.f2_shard_rows;
-        const long row0 = (long)(m0 - owner * args.f2_shard_rows) + quarter * 32;  // shard row of lane-row 0
-        float* base = reinterpret_cast<float*>(args.f2_base32[owner]);
-        float* inbox = base + args.f2_grad_off;  // [src][shard]
-        // one counter per 128-row half tile (identical numbering for single CTAs and pairs)
-        int* cnt = reinterpret_cast<int*>(base + args.f2_cnt_off) + (mt * (TILE_M / BM) + (int)cta_rank) * sched.n_tiles + nt;
-        const float* local_grad = reinterpret_cast<const float*>(args.out);
-        float* stg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full_bar) + 256) + (warp - 2) * 1024;
-        const int rsub = lane >> 3, slot = lane & 7;
-        const bool is_owner = owner == args.f2_rank;
-        if (is_owner && !warp_wait_count_sys(cnt, EPI_WARPS * (args.f2_world - 1))) {
-          report_error(args.err, kErrPeerWaitTimeout, 6);
-          return false;
-        }
-        const float lr = args.f2_hyper[0], inv_bc1 = args.f2_hyper[1], inv_bc2s = args.f2_hyper[2];
-        const float b1 = args.f2_beta1, b2 = args.f2_beta2, wd = args.f2_wd, ed = args.f2_ema;
-        float* mine = inbox + (long)args.f2_rank * args.f2_inbox_stride;
-#pragma unroll 1
-        for (int c = half * 4; c < half * 4 + 4; ++c) {
-          float v[32];
-          tmem_load_f32x32(taddr + c * 32, v);
-          const int n = nt * BN + c * 32;
-          __syncwarp();
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(stg + lane * 32 + ((q ^ (lane & 7)) << 2)) =
-                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          __syncwarp();
-          if (n >= args.N) continue;  // warp-uniform
-#pragma unroll 2
-          for (int i = 0; i < 8; ++i) {
-            const int r = i * 4 + rsub;
-            const int gm = m0 + quarter * 32 + r;
-            if (gm >= args.M) continue;
-            float4 g4 = *reinterpret_cast<const float4*>(stg + r * 32 + ((slot ^ (r & 7)) << 2));
-            const int col = n + slot * 4;
-            const float4 lg = *reinterpret_cast<const float4*>(local_grad + (long)gm * args.ldo + col);
-            g4.x += lg.x; g4.y += lg.y; g4.z += lg.z; g4.w += lg.w;
-            const long idx = (row0 + r) * args.f2_cols + col;
-            if (!is_owner) {
-              *reinterpret_cast<float4*>(mine + idx) = g4;
-              continue;
-            }
-            for (int src = 0; src < args.f2_world; ++src) {
-              if (src == args.f2_rank) continue;
-              const float4 t = *reinterpret_cast<const float4*>(inbox + (long)src * args.f2_inbox_stride + idx);
-              g4.x += t.x; g4.y += t.y; g4.z += t.z; g4.w += t.w;
-            }
-            float* pm = base + args.f2_master_off + idx;
-            float* pv = base + args.f2_v_off + idx;
-            float* pmo = base + args.f2_m_off + idx;
-            float4 p4 = *reinterpret_cast<float4*>(pm);
-            float4 v4 = *reinterpret_cast<float4*>(pv);
-            float4 m4 = args.f2_has_m ? *reinterpret_cast<float4*>(pmo) : make_float4(0.f, 0.f, 0.f, 0.f);
-            float* pp = &p4.x; float* vv = &v4.x; float* mm = &m4.x;
-            const float* gg = &g4.x;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float pe_ = pp[e];
-              if (wd != 0.f) pe_ *= 1.f - lr * wd;
-              vv[e] = b2 * vv[e] + (1.f - b2) * gg[e] * gg[e];
-              const float denom = sqrtf(vv[e]) * inv_bc2s;
-              float upd;
-              if (args.f2_has_m) {
-                mm[e] = mm[e] + (1.f - b1) * (gg[e] - mm[e]);
-                upd = atan2f(mm[e], denom) * (lr * inv_bc1);
-              } else {
-                upd = atan2f(gg[e], denom) * lr;
-              }
-              pp[e] = pe_ - upd;
-            }
-            *reinterpret_cast<float4*>(pm) = p4;
-            *reinterpret_cast<float4*>(pv) = v4;
-            if (args.f2_has_m) *reinterpret_cast<float4*>(pmo) = m4;
-            if (args.f2_has_ema) {
-              float* pe = base + args.f2_ema_off + idx;
-              float4 e4 = *reinterpret_cast<float4*>(pe);
-              e4.x += (1.f - ed) * (p4.x - e4.x); e4.y += (1.f - ed) * (p4.y - e4.y);
-              e4.z += (1.f - ed) * (p4.z - e4.z); e4.w += (1.f - ed) * (p4.w - e4.w);
-              *reinterpret_cast<float4*>(pe) = e4;
-            }
-            __nv_bfloat16* p16 = reinterpret_cast<__nv_bfloat16*>(args.f2_base16[owner]) + args.f2_s16_off + idx;
-            *reinterpret_cast<uint2*>(p16) = make_uint2(pack_bf16x2(p4.x, p4.y), pack_bf16x2(p4.z, p4.w));
-          }
-        }
-        if (!is_owner) {
-          __threadfence_system();
-          __syncwarp();
-          if (lane == 0) atomicAdd_system(cnt, 1);
-        }
       } else if constexpr (EPI == EPI_CE_BWD) {
         // Logits of one V chunk (columns [col0, col0 + N) of the head), recomputed by this GEMM
         // and rounded to bf16 exactly as the forward's statistics saw them, turned into
@@ -870,7 +721,7 @@ int max_pair_clusters() {
   TORCH_CHECK(dev < kMaxDevices, "device index out of range");
   int n = per_device[dev].load(std::memory_order_acquire);
   if (n == 0) {
-    auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 0, 1>;
+    auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 1>;
     TORCH_CHECK(ensure_dynamic_smem((const void*)kern, pair_smem_bytes<EPI>()) == cudaSuccess,
                 "cudaFuncSetAttribute failed");
     cudaLaunchConfig_t cfg = {};
@@ -896,7 +747,7 @@ int max_pair_clusters() {
 template <int A_MN, int B_MN, int EPI>
 void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int clusters,
                  cudaStream_t stream) {
-  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 0, 1>;
+  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 1>;
   max_pair_clusters<A_MN, B_MN, EPI>();  // sets the shared-memory attribute
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
@@ -914,9 +765,9 @@ void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int A_MN, int B_MN, int EPI, int F1 = 0>
+template <int A_MN, int B_MN, int EPI>
 void launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int grid, cudaStream_t stream) {
-  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, F1>;
+  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI>;
   TORCH_CHECK(ensure_dynamic_smem((const void*)kern, gemm_smem_bytes<EPI>()) == cudaSuccess,
               "cudaFuncSetAttribute failed");
   kern<<<grid, GEMM_THREADS, gemm_smem_bytes<EPI>(), stream>>>(ma, mb, args);
@@ -926,6 +777,7 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, 
 }  // namespace
 
 at::Tensor device_error_word();  // errors.cu
+CopyJobs decode_copy_jobs(const at::Tensor& d);
 
 // Generic entry: see the file header for operand conventions.
 //   a: [M,K] (a_mn=0) or [K,M] (a_mn=1);  b: [Nb,K] (b_mn=0) or [K,N] (b_mn=1)
@@ -936,7 +788,8 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
           const c10::optional<at::Tensor>& sin_tab, int64_t rope_begin, int64_t rope_end, int64_t pair_offset,
           const c10::optional<at::Tensor>& labels, const c10::optional<at::Tensor>& ce_max,
           const c10::optional<at::Tensor>& ce_sum, const c10::optional<at::Tensor>& ce_arg,
-          const c10::optional<at::Tensor>& ce_tgt, bool stream_k, int64_t splitk) {
+          const c10::optional<at::Tensor>& ce_tgt, bool stream_k, int64_t splitk,
+          const c10::optional<at::Tensor>& jobs) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm: row-major 2D operands");
   TORCH_CHECK(N % 32 == 0, "gemm: N must be a multiple of 32");
@@ -982,6 +835,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   if (ce_arg) args.ce_arg = ce_arg->data_ptr<int>();
   if (ce_tgt) args.ce_tgt = ce_tgt->data_ptr<float>();
   args.err = device_error_word().data_ptr<int>();
+  if (jobs) args.jobs = decode_copy_jobs(*jobs);
   args.stream_k = stream_k ? 1 : 0;
   // fp32 weight gradients with a long K (tokens): split K into chunks whose operand slices
   // (both [chunk, M] and [chunk, N] panels, ~48 MB) fit in L2 next to the accumulation traffic
@@ -1056,117 +910,31 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   TORCH_CHECK(false, "gemm: unsupported (a_mn, b_mn, epilogue) combination ", a_mn, b_mn, epi);
 }
 
-
-
-// ---------------------------------------------------------------------------------------
-// Fused-collective GEMMs (multi-GPU sharding engine)
-// ---------------------------------------------------------------------------------------
-// Encode `world` tensor maps, one per rank's bf16 shard [shard_rows, cols] of a weight,
-// from the shards' device addresses (this rank's own and its peers'). Returns a CPU uint8
-// tensor holding the CUtensorMap array (copy it to the device before use).
-at::Tensor encode_shard_maps(const std::vector<int64_t>& shard_addrs, int64_t shard_rows, int64_t cols) {
-  const int world = (int)shard_addrs.size();
-  at::Tensor out = at::empty({(int64_t)(world * sizeof(CUtensorMap))}, at::TensorOptions().dtype(at::kByte));
-  CUtensorMap* maps = reinterpret_cast<CUtensorMap*>(out.data_ptr());
-  TORCH_CHECK((cols * 2) % 16 == 0, "shard rows must be 16-byte aligned");
-  for (int r = 0; r < world; ++r) {
-    TORCH_CHECK((shard_addrs[r] & 15) == 0, "shard base must be 16-byte aligned");
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)shard_rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
-    cuuint32_t box[2] = {64, 128};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult res = encode_fn()(&maps[r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                               reinterpret_cast<void*>(shard_addrs[r]), dims, strides, box, estr,
-                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    TORCH_CHECK(res == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)res);
+// Fused-collective copy jobs for one launch (collective_jobs.cuh), from a CPU int64 [16]
+// descriptor: {gather: src addresses tensor ptr, dst ptr, rows, cols, rows per rank;
+// push: src ptr, base addresses tensor ptr, inbox offset, inbox slot stride, count offset,
+// rows, cols, rows per rank, rank, ran-flag ptr; unused}. Addresses are device pointers.
+CopyJobs decode_copy_jobs(const at::Tensor& d) {
+  TORCH_CHECK(!d.is_cuda() && d.scalar_type() == at::kLong && d.numel() == 16, "copy jobs: CPU int64 [16] expected");
+  const int64_t* v = d.data_ptr<int64_t>();
+  CopyJobs j{};
+  if (v[0] != 0) {
+    j.g_src = reinterpret_cast<const unsigned long long*>(v[0]);
+    j.g_dst = reinterpret_cast<__nv_bfloat16*>(v[1]);
+    j.g_rows = (int)v[2]; j.g_cols = (int)v[3]; j.g_chunk = (int)v[4];
+    TORCH_CHECK(j.g_cols % 8 == 0 && j.g_chunk > 0 && (v[1] & 15) == 0, "gather job: 16-byte aligned rows expected");
   }
-  return out;
-}
-
-// F1: x [M,K] @ w^T with the weight's rows gathered on the fly from the owners' shards
-// (peer_maps, device) into the resident local copy `w`; epilogue ROPE or SWIGLU.
-void gemm_f1(const at::Tensor& x, const at::Tensor& w, int64_t M, int64_t N, int64_t K, int64_t epi,
-             const at::Tensor& out, const c10::optional<at::Tensor>& out2, const c10::optional<at::Tensor>& positions,
-             const c10::optional<at::Tensor>& cos_tab, const c10::optional<at::Tensor>& sin_tab, int64_t rope_begin,
-             int64_t rope_end, int64_t pair_offset, const at::Tensor& peer_maps, int64_t shard_rows,
-             const at::Tensor& flags) {
-  c10::cuda::CUDAGuard guard(x.device());
-  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  TORCH_CHECK(shard_rows % 128 == 0, "F1 needs shards of a multiple of 128 rows");
-  TORCH_CHECK(peer_maps.is_cuda() && (reinterpret_cast<uintptr_t>(peer_maps.data_ptr()) & 63) == 0,
-              "peer tensor maps must live in 64-byte aligned device memory");
-  GemmArgs args{};
-  args.M = (int)M; args.N = (int)N; args.K = (int)K;
-  args.out = out.data_ptr(); args.ldo = out.stride(0);
-  if (out2) { args.out2 = out2->data_ptr(); args.ldo2 = out2->stride(0); }
-  if (positions) args.positions = positions->data_ptr<int>();
-  if (cos_tab) {
-    args.cos_tab = cos_tab->data_ptr<float>();
-    args.rope_rows = (int)cos_tab->size(0);
+  if (v[5] != 0) {
+    j.p_src = reinterpret_cast<const float*>(v[5]);
+    j.p_base = reinterpret_cast<const unsigned long long*>(v[6]);
+    j.p_inbox_off = v[7]; j.p_inbox_stride = v[8]; j.p_cnt_off = v[9];
+    j.p_rows = (int)v[10]; j.p_cols = (int)v[11]; j.p_chunk = (int)v[12]; j.p_rank = (int)v[13];
+    j.p_ran = reinterpret_cast<int*>(v[14]);
+    TORCH_CHECK(j.p_rows % 32 == 0 && j.p_cols % 4 == 0 && j.p_chunk % 32 == 0 && (v[5] & 15) == 0 &&
+                    j.p_inbox_off % 4 == 0 && j.p_inbox_stride % 4 == 0,
+                "push job: 32-row groups of 16-byte aligned fp32 rows expected");
   }
-  if (sin_tab) args.sin_tab = sin_tab->data_ptr<float>();
-  args.rope_begin = (int)rope_begin; args.rope_end = (int)rope_end; args.pair_offset = (int)pair_offset;
-  args.err = device_error_word().data_ptr<int>();
-  args.f1_peer_maps = reinterpret_cast<const CUtensorMap*>(peer_maps.data_ptr());
-  args.f1_shard_rows = (int)shard_rows;
-  args.f1_flags = flags.data_ptr<int>();
-  CUtensorMap ma = make_map(x, K, M, x.stride(0), 64, 128);
-  CUtensorMap mb = make_map(w, K, w.size(0), w.stride(0), 64, 128);
-  const int64_t n_tiles = (epi == EPI_SWIGLU) ? (N + 127) / 128 : (N + BN - 1) / BN;
-  TORCH_CHECK(flags.numel() >= n_tiles, "F1 flag buffer too small");
-  const int64_t tiles = ((M + BM - 1) / BM) * n_tiles;
-  const int grid = (int)std::min<int64_t>(tiles, num_sms());
-  TORCH_CHECK(n_tiles <= grid, "F1 writer tiles must all be resident in the first wave");
-  if (epi == EPI_ROPE) return launch<0, 0, EPI_ROPE, 1>(ma, mb, args, grid, stream);
-  if (epi == EPI_SWIGLU) return launch<0, 0, EPI_SWIGLU, 1>(ma, mb, args, grid, stream);
-  if (epi == EPI_STORE) return launch<0, 0, EPI_STORE, 1>(ma, mb, args, grid, stream);
-  TORCH_CHECK(false, "gemm_f1: unsupported epilogue ", epi);
-}
-
-// F2: dW = dy^T x (dy [T,M] MN-major, x [T,N] MN-major) for the final backward contribution:
-// each complete tile (+ local_grad, the local partial of earlier calls) is stored into this
-// rank's slot of the owner's fp32 inbox over NVLink, and the last arrival per tile reduces the
-// slots and runs the owner's AdamATan2 update, all in this kernel.
-// offsets (CPU int64[7]): inbox (slot 0, this weight), master, exp_avg, exp_avg_sq, ema (fp32
-// elements), shard16 (bf16 elements), counters (int32 elements) -- identical on every rank.
-void gemm_f2(const at::Tensor& dy, const at::Tensor& x, int64_t M, int64_t N, int64_t K, const at::Tensor& local_grad,
-             const at::Tensor& base32, const at::Tensor& base16, const std::vector<int64_t>& offsets,
-             int64_t shard_rows, int64_t inbox_stride, int64_t rank, int64_t world, const at::Tensor& hyper,
-             double beta1, double beta2, double wd, double ema_decay, bool has_m, bool has_ema) {
-  c10::cuda::CUDAGuard guard(dy.device());
-  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  TORCH_CHECK(shard_rows % BM == 0, "F2 needs shards of a multiple of 128 rows");
-  TORCH_CHECK(offsets.size() == 7, "offsets: inbox, master, m, v, ema, s16, counters");
-  GemmArgs args{};
-  args.M = (int)M; args.N = (int)N; args.K = (int)K;
-  args.out = local_grad.data_ptr(); args.ldo = local_grad.stride(0);
-  args.err = device_error_word().data_ptr<int>();
-  args.f2_split = 1; args.f2_world = (int)world; args.f2_shard_rows = (int)shard_rows; args.f2_cols = (int)N;
-  args.f2_inbox_stride = inbox_stride; args.f2_rank = (int)rank;
-  TORCH_CHECK(N % 32 == 0 && shard_rows % BM == 0, "F2 needs N % 32 == 0 and shard rows % 128 == 0");
-  args.f2_base32 = reinterpret_cast<const unsigned long long*>(base32.data_ptr<int64_t>());
-  args.f2_base16 = reinterpret_cast<const unsigned long long*>(base16.data_ptr<int64_t>());
-  args.f2_grad_off = offsets[0]; args.f2_master_off = offsets[1]; args.f2_m_off = offsets[2];
-  args.f2_v_off = offsets[3]; args.f2_ema_off = offsets[4]; args.f2_s16_off = offsets[5]; args.f2_cnt_off = offsets[6];
-  args.f2_hyper = hyper.data_ptr<float>();
-  args.f2_beta1 = (float)beta1; args.f2_beta2 = (float)beta2; args.f2_wd = (float)wd; args.f2_ema = (float)ema_decay;
-  args.f2_has_m = has_m ? 1 : 0; args.f2_has_ema = has_ema ? 1 : 0;
-  CUtensorMap ma = make_map(dy, M, K, dy.stride(0), 64, 64);
-  CUtensorMap mb = make_map(x, N, K, x.stride(0), 64, 64);
-  static const bool pair_enabled = [] {
-    const char* v = std::getenv("HRM_GEMM_PAIR");
-    return v == nullptr || std::string(v) != "0";
-  }();
-  if (pair_enabled && M >= 1024) {  // every rank computes the same launch shape (same tile order)
-    const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
-    const int clusters = (int)std::min<int64_t>(tiles, max_pair_clusters<1, 1, EPI_F2>());
-    launch_pair<1, 1, EPI_F2>(ma, mb, args, clusters, stream);
-    return;
-  }
-  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = (int)std::min<int64_t>(tiles, num_sms());
-  launch<1, 1, EPI_F2>(ma, mb, args, grid, stream);
+  return j;
 }
 
 }  // namespace hrm

@@ -213,23 +213,12 @@ __global__ void adam_atan2_kernel(float* __restrict__ p, const float* __restrict
                                   float ema_decay) {
   const float lr = hyper[0], inv_bc1 = hyper[1], inv_bc2_sqrt = hyper[2];
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    float pv = p[i];
-    const float gv = g[i];
-    if (wd != 0.f) pv *= 1.f - lr * wd;
     float vv = v[i];
-    vv = beta2 * vv + (1.f - beta2) * gv * gv;
+    float mv = m != nullptr ? m[i] : 0.f;
+    const float pv = adam_atan2_update(p[i], g[i], m != nullptr, mv, vv, lr, inv_bc1, inv_bc2_sqrt, beta1,
+                                       beta2, wd);
     v[i] = vv;
-    const float denom = sqrtf(vv) * inv_bc2_sqrt;
-    float upd;
-    if (m != nullptr) {
-      float mv = m[i];
-      mv = mv + (1.f - beta1) * (gv - mv);
-      m[i] = mv;
-      upd = atan2f(mv, denom) * (lr * inv_bc1);
-    } else {
-      upd = atan2f(gv, denom) * lr;
-    }
-    pv -= upd;
+    if (m != nullptr) m[i] = mv;
     p[i] = pv;
     if (ema != nullptr) {
       float e = ema[i];

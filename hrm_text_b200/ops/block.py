@@ -24,6 +24,7 @@ import torch
 from torch import Tensor
 
 from .._native import cuda
+from ..parallel.fused import before_use
 from ..utils.trace import nvtx
 from . import gemm as G
 from .attention import PackedSeq, attention_bwd, attention_fwd, rope_half_tables
@@ -53,8 +54,9 @@ def _wgrad(dy: Tensor, x: Tensor, w: Tensor, grads: list, idx: int) -> None:
     f2 = getattr(w, "_f2", None)
     if f2 is not None:
         w._f2_pending -= 1
-        if f2.enabled and w._f2_pending == 0:  # last contribution of this step: reduce-scatter + update
-            G.linear_wgrad_f2(dy, x, w.main_grad, f2)
+        if f2.enabled and w._f2_pending == 0:  # last contribution of this step
+            G.linear_wgrad_(dy, x, w.main_grad)
+            f2.owner.queue_push(f2)  # the next GEMM pushes the finished rows to their owners
             return
     main = getattr(w, "main_grad", None)
     if main is not None:
@@ -74,21 +76,23 @@ class FusedPreNormBlock(torch.autograd.Function):
         with nvtx("rmsnorm.fwd"):
             xn, r1, s = rmsnorm(x, eps, injection)
         sched = packed.schedule(causal)
-        f1_qkv, f1_gu = getattr(w_gqkv, "_f1", None), getattr(w_gu, "_f1", None)
+        # multi-GPU fused path: before_use makes sure a sharded weight's resident copy is gathered
+        # (normally by a copy job inside an earlier GEMM of the step) before its first GEMM
         with nvtx("gemm.gqkv_rope"):
-            if f1_qkv is None:
-                gqkv = G.linear_rope(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden)
-            else:
-                gqkv = G.linear_rope_f1(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden, f1_qkv)
+            before_use(w_gqkv)
+            gqkv = G.linear_rope(xn, w_gqkv, packed.position_ids, cos, sin, hidden, 3 * hidden)
         with nvtx("attention.fwd"):
             o, y, lse = attention_fwd(gqkv, num_heads, sched)
         with nvtx("gemm.o_residual"):
+            before_use(w_o)
             x1 = G.linear(y, w_o, residual=s)
         with nvtx("rmsnorm.fwd"):
             xn2, r2, _ = rmsnorm(x1, eps)
         with nvtx("gemm.gate_up_swiglu"):
-            gu, h = G.linear_swiglu(xn2, w_gu) if f1_gu is None else G.linear_swiglu_f1(xn2, w_gu, f1_gu)
+            before_use(w_gu)
+            gu, h = G.linear_swiglu(xn2, w_gu)
         with nvtx("gemm.down_residual"):
+            before_use(w_d)
             x2 = G.linear(h, w_d, residual=x1)
         if train:
             for w in (w_gqkv, w_o, w_gu, w_d):

@@ -17,7 +17,18 @@ from torch import Tensor
 
 from .._native import cuda
 
-EPI_STORE, EPI_RESIDUAL, EPI_F32ADD, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_CE, EPI_F2, EPI_CE_BWD = range(9)
+EPI_STORE, EPI_RESIDUAL, EPI_F32ADD, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_CE = range(7)
+EPI_CE_BWD = 8
+
+# Fused collectives (multi-GPU engine): a registered job source hands every GEMM launch the
+# copy jobs (weight gather ahead of its first use, gradient push to the owners) that its
+# epilogue warps run before their first tile; see hrm_text_b200.parallel.fused.
+_job_source = None
+
+
+def set_job_source(fn) -> None:
+    global _job_source
+    _job_source = fn
 
 
 def _check(*tensors: Tensor) -> None:
@@ -31,8 +42,9 @@ def _check(*tensors: Tensor) -> None:
 def _gemm(a, a_mn, b, b_mn, M, N, K, epi, out, out2=None, residual=None, aux=None, positions=None, cos=None,
           sin=None, rope_begin=0, rope_end=0, pair_offset=0, labels=None, ce_max=None, ce_sum=None, ce_arg=None,
           ce_tgt=None, stream_k=False, splitk=0):
+    jobs = _job_source() if _job_source is not None else None
     cuda().gemm(a, a_mn, b, b_mn, M, N, K, epi, out, out2, residual, aux, positions, cos, sin, rope_begin, rope_end,
-                pair_offset, labels, ce_max, ce_sum, ce_arg, ce_tgt, stream_k, splitk)
+                pair_offset, labels, ce_max, ce_sum, ce_arg, ce_tgt, stream_k, splitk, jobs)
 
 
 def linear(x: Tensor, w: Tensor, out: Optional[Tensor] = None, residual: Optional[Tensor] = None) -> Tensor:
@@ -195,42 +207,3 @@ def infer_swiglu(x: Tensor, w: Tensor) -> Tensor:
     h = torch.empty((x.shape[0], inter), dtype=torch.bfloat16, device=x.device)
     cuda().decode_linear_finish(acc, EPI_SWIGLU, h, None, None, None, None, 0, 0, inter)
     return h
-
-
-# ---------------------------------------------------------------------------------------
-# fused-collective variants (multi-GPU sharding engine; see hrm_text_b200.parallel.fused)
-# ---------------------------------------------------------------------------------------
-def linear_rope_f1(x: Tensor, w: Tensor, positions: Tensor, cos: Tensor, sin: Tensor, rope_begin: int,
-                   rope_end: int, f1) -> Tensor:
-    """``linear_rope`` whose weight rows are gathered from their owners' shards in the same kernel."""
-    _check(x, w)
-    M, K = x.shape
-    N = w.shape[0]
-    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
-    cuda().gemm_f1(x, w, M, N, K, EPI_ROPE, out, None, positions, cos, sin, rope_begin, rope_end, 0, f1.maps,
-                   f1.shard_rows, f1.flags)
-    return out
-
-
-def linear_swiglu_f1(x: Tensor, w: Tensor, f1) -> tuple[Tensor, Tensor]:
-    """``linear_swiglu`` with the weight gathered from its owners' shards in the same kernel."""
-    _check(x, w)
-    M, K = x.shape
-    inter = w.shape[0] // 2
-    gu = torch.empty((M, 2 * inter), dtype=torch.bfloat16, device=x.device)
-    h = torch.empty((M, inter), dtype=torch.bfloat16, device=x.device)
-    cuda().gemm_f1(x, w, M, inter, K, EPI_SWIGLU, gu, h, None, None, None, 0, 0, inter, f1.maps, f1.shard_rows,
-                   f1.flags)
-    return gu, h
-
-
-def linear_wgrad_f2(dy: Tensor, x: Tensor, local_grad: Tensor, f2) -> None:
-    """Final weight-gradient GEMM of a step: ``local_grad + dy.T @ x`` is reduced into the
-    owners' shards and the owners' AdamATan2 update runs in the same kernel."""
-    _check(dy, x)
-    T, N = dy.shape
-    K = x.shape[1]
-    fc = f2.owner
-    base32, base16, hyper, b1, b2, wd, ema, has_m, has_ema = fc.f2_kernel_args()
-    cuda().gemm_f2(dy, x, N, K, T, local_grad, base32, base16, f2.offsets, f2.shard_rows, fc.params.shard_numel,
-                   fc.rank, fc.world, hyper, b1, b2, wd, ema, has_m, has_ema)

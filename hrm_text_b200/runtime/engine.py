@@ -104,10 +104,9 @@ class ShardedParameters:
         f32 = dict(dtype=torch.float32, device=dev)
         self.hyper = torch.zeros(4, **f32)  # lr, 1/bc1, 1/sqrt(bc2)
         if fused is None:
-            # F1/F2 fused collectives are opt-in: with CTA-pair GEMMs elsewhere, the plain NCCL
-            # path is faster end to end on one node (measured: 2 x B200, HRM-Text L, 300.0 ms
-            # vs 319.5 ms per step)
-            fused = os.environ.get("HRM_FUSED_COLLECTIVES", "0") == "1"
+            # F1/F2 fused collectives (parallel/fused.py) are the default multi-GPU path;
+            # HRM_FUSED_COLLECTIVES=0 selects the plain NCCL reduce-scatter / all-gather baseline
+            fused = os.environ.get("HRM_FUSED_COLLECTIVES", "1") == "1"
         self.fused = None
         if fused and self.world > 1 and self.on_cuda:
             # F1/F2: optimizer state, gradient shard and bf16 shards in peer-addressable memory
@@ -221,16 +220,7 @@ class ShardedParameters:
 
     def optimizer_step(self) -> None:
         if self.on_cuda and self.fused is not None:
-            from .._native import cuda
-            for s in self.slots:
-                if self._is_f2(s):
-                    continue  # updated inside the fused wgrad kernel
-                sl = slice(s.shard_off, s.shard_off + s.shard_numel)
-                cuda().adam_atan2(self.master[sl], self.grad_shard[sl],
-                                  None if self.exp_avg is None else self.exp_avg[sl], self.exp_avg_sq[sl],
-                                  None if self.param_ema is None else self.param_ema[sl], self.shard16[sl],
-                                  self.hyper, self.beta1, self.beta2, self.weight_decay,
-                                  self.ema if self.ema is not None else 0.0)
+            self.fused.update()  # F2 inbox reduction + AdamATan2 for every local shard, one kernel
             return
         if self.on_cuda:
             from .._native import cuda
@@ -254,7 +244,8 @@ class ShardedParameters:
         """Distribute the updated bf16 shards to every rank's resident compute buffer.
 
         With fused collectives, F1 weights are gathered by their first GEMM of the next step
-        instead (unless ``all_slots``).
+        instead (unless ``all_slots``); call ``sync_compute`` before using the model outside a
+        training step.
         """
         if self.world == 1:
             if self.step_count == 0:  # initial fill
@@ -281,6 +272,12 @@ class ShardedParameters:
                 view[self.rank].copy_(self.shard16[s.shard_off: s.shard_off + s.shard_numel])
             dist.all_reduce(full, op=dist.ReduceOp.SUM, group=self.group)
             self.compute.copy_(full)
+
+    def sync_compute(self) -> None:
+        """Bring the resident compute weights up to date outside a training step (the F1
+        weights are otherwise gathered lazily by the next step's first GEMMs)."""
+        if self.fused is not None and self.fused.f1:
+            self.gather_params(all_slots=True)
 
     # ------------------------------------------------------------------ state access
     def full_param_fp32(self, s: ParamSlot, buf: Optional[Tensor] = None) -> Tensor:
@@ -328,6 +325,8 @@ class TrainEngine:
             self.carry, loss, metrics = self.model(carry=self.carry, batch=batch, **extra)
         with nvtx("backward"):
             loss.backward()
+        if self.params.fused is not None:
+            self.params.fused.flush()  # gradient pushes that no backward GEMM carried
         self.params.collect_autograd_grads()
         return loss.detach(), metrics
 

@@ -63,6 +63,12 @@ class Trainer:
         loss, _ = self.train_step_async(batch, lr, bp_steps)
         return float(loss.item())
 
+    def sync_weights(self) -> None:
+        """Make ``self.model``'s weights current for use outside ``train_step`` (inference,
+        evaluation). On several GPUs the block weights are gathered lazily by the next step's
+        first GEMMs, so between steps the resident copies of those weights lag one update."""
+        self.engine.params.sync_compute()
+
     def close(self) -> None:
         if self._graphed is not None:
             self._graphed.release()

@@ -1,6 +1,10 @@
-"""Multi-GPU (2 ranks, NCCL): the fused-collective engine (F1 all-gather fused into the
-QKV / gate-up GEMMs, F2 wgrad + reduce-scatter + AdamATan2 in one kernel) must train
-exactly like the plain NCCL engine. Skipped with fewer than 2 GPUs."""
+"""Multi-GPU (2 ranks, NCCL): the fused-collective engine (F1: all-gather inside the first GEMM
+of a step that reads each block weight; F2: the last weight-gradient GEMM pushes finished
+gradient regions to their owners, and one step-end kernel sums them and runs AdamATan2) must
+train like the plain NCCL engine (HRM_FUSED_COLLECTIVES=0), eager and CUDA-graphed. The
+steps alternate bp_steps 3 and 1: with one backward call the L module's weights get no
+gradient in that step, so their F2 GEMMs do not run and the owners must not wait for them.
+Skipped with fewer than 2 GPUs."""
 import os
 
 import pytest
@@ -10,7 +14,7 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-STEPS = 3
+BP_STEPS = (3, 1, 3)
 
 
 def _cfg():
@@ -34,15 +38,15 @@ def _worker(rank, world, fused, graphed, out, port):
         eng = TrainEngine(build_model(_cfg(), torch.device("cuda", rank)), beta1=0.9, beta2=0.95, weight_decay=0.1,
                           ema=0.99)
         assert (eng.params.fused is not None) == fused
-        batches = [b for b, _ in packed_batches(1024, 1024, 1024, rank=rank, world=world, num_batches=STEPS,
+        batches = [b for b, _ in packed_batches(1024, 1024, 1024, rank=rank, world=world, num_batches=len(BP_STEPS),
                                                  median=256.0)]
         runner = GraphedTrainStep(eng, batches[0]) if graphed else None
         losses = []
-        for b in batches:
+        for b, bp in zip(batches, BP_STEPS):
             if graphed:
-                loss, _ = runner(b, lr=1e-3, bp_steps=3)
+                loss, _ = runner(b, lr=1e-3, bp_steps=bp)
             else:
-                loss, _ = eng.train_step({k: v.cuda() for k, v in b.items()}, lr=1e-3, bp_steps=3)
+                loss, _ = eng.train_step({k: v.cuda() for k, v in b.items()}, lr=1e-3, bp_steps=bp)
             losses.append(float(loss))
         torch.cuda.synchronize()
         check_device_errors()
