@@ -580,7 +580,7 @@ __global__ void zero_tail_kernel(__nv_bfloat16* out, __nv_bfloat16* y, long ld_o
 // so the softmax of b+1 overlaps the tensor-core work of b (two TMEM regions).
 // Warp roles (320 threads): 0 TMA, 1 UMMA, 2..9 compute. Compute warp group g (warps 2-5,
 // 6-9) owns queries [32g, 32g+32) of every block: the softmax of that half (two warps per
-// scheduler), then, after writing the next block's P^T / dS^T, that half of dQ^T, which it
+// scheduler), then, before writing that block's P^T / dS^T, the previous block's dQ^T, which it
 // moves from TMEM through a warp-private shared-memory box into the fp32 dQ accumulator with
 // one tensor reduction per warp and block (cp.reduce.async.bulk.tensor .add, [32 x 32] fp32).
 // P^T / dS^T tiles are double-buffered by block parity, so a block's softmax only waits for
@@ -672,7 +672,7 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ int bwd_qstart(const int4& t) { return t.w < t.z ? 0 : t.w; }
@@ -1011,12 +1011,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           }
         }
         pc.mark(1);
+        // dQ^T of block b - 1 first (its UMMAs ran while this block's softmax did): that frees
+        // the TMEM region the UMMAs of block b + 1 need; its staging is pair (b - 1) & 1, not
+        // the pair P^T(b) goes to
+        if (qb > 0 && !drain_dq(b - 1, t, head, qbase - BQB)) { ok = false; break; }
         // pair b & 1 was last read by the UMMAs of block b - 2 ...
         if (!warp_wait(&bar->p_free[b & 1], ((b >> 1) & 1) ^ 1)) { report_error(p.err, kErrAttnWaitTimeout, 62); ok = false; break; }
         // ... and staged dQ^T(b - 2) for every warp's reduction
         if (b >= 2) {
           if (lane == 0) {
-            bulk_wait_group_read0();  // this warp's reduction of dQ^T(b - 2), its latest, has read its box
+            // this warp's reduction of dQ^T(b - 2) has read its box (dQ^T(b - 1), committed
+            // after it, may still be reading)
+            bulk_wait_group_read1();
             mbar_arrive(&bar->stage_free[b & 1]);
           }
           if (!warp_wait(&bar->stage_free[b & 1], ((b - 2) >> 1) & 1)) { report_error(p.err, kErrAttnWaitTimeout, 64); ok = false; break; }
@@ -1034,8 +1040,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tc_fence_before();
         mbar_arrive(&bar->p_full[b & 1]);
         pc.mark(3);
-        // dQ^T of block b - 1, whose UMMAs ran while this block's softmax did
-        if (qb > 0 && !drain_dq(b - 1, t, head, qbase - BQB)) { ok = false; break; }
       }
       if (!ok) break;
       if (!drain_dq(b - 1, t, head, qs + (nqb - 1) * BQB)) { ok = false; break; }

@@ -4,7 +4,8 @@
 
 Each case is timed with CUDA events over ``iters`` launches after warm-up; reports TFLOP/s.
 Cases: the forward GEMMs of a layer (RoPE, SwiGLU, residual epilogues), their dgrad GEMMs
-(SwiGLU-backward epilogue for the down projection) and the fp32 weight-gradient GEMMs.
+(SwiGLU-backward epilogue for the down projection), the fp32 weight-gradient GEMMs, and the
+LM-head GEMM with the cross-entropy statistics epilogue (vocabulary 32768, logits not stored).
 """
 from __future__ import annotations
 
@@ -44,6 +45,9 @@ def main(argv=None):
     dy_qkv = rnd(T, 4 * h, scale=0.01)
     grad_qkv = torch.zeros(4 * h, h, device=dev)
     grad_d = torch.zeros(h, inter, device=dev)
+    vocab = 32768
+    w_head = rnd(vocab, h, scale=0.02)
+    labels = torch.randint(0, vocab, (T,), device=dev, dtype=torch.int32)
     cases = {
         "qkv_rope": (lambda: G.linear_rope(x, w_qkv, pos, cos, sin, h, 3 * h), 2 * T * 4 * h * h),
         "o_residual": (lambda: G.linear(x, w_o, residual=x), 2 * T * h * h),
@@ -53,6 +57,7 @@ def main(argv=None):
         "qkv_dgrad": (lambda: G.linear_dgrad(dy_qkv, w_qkv), 2 * T * 4 * h * h),
         "qkv_wgrad": (lambda: G.linear_wgrad_(dy_qkv, x, grad_qkv), 2 * T * 4 * h * h),
         "down_wgrad": (lambda: G.linear_wgrad_(dy_h, hmid, grad_d), 2 * T * h * inter),
+        "lm_head_ce": (lambda: G.lm_head_ce_stats(x, w_head, labels), 2 * T * vocab * h),
     }
     results = {}
     for name, (fn, flop) in cases.items():
