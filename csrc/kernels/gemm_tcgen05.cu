@@ -441,17 +441,34 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
       if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-#pragma unroll 1
-        for (int c = half * 4; c < half * 4 + 4; ++c) {
+        // residual: all four chunks' rows are requested before the first TMEM load, so their
+        // latency overlaps instead of being paid once per chunk
+        uint4 rraw[EPI == EPI_RESIDUAL ? 16 : 1];
+        if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int n = nt * BN + (half * 4 + q) * 32;
+            const uint4* src = reinterpret_cast<const uint4*>(args.residual + (long)m * args.ldr + n);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) rraw[4 * q + i] = (row_ok && n < args.N) ? src[i] : make_uint4(0, 0, 0, 0);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = half * 4 + q;
           float v[32];
           tmem_load_f32x32(taddr + c * 32, v);
           const int n = nt * BN + c * 32;
           if (row_ok && n < args.N) {
             if constexpr (EPI == EPI_RESIDUAL) {
-              float rsd[32];
-              load_bf16x32(args.residual + (long)m * args.ldr + n, rsd);
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += rsd[j];
+              for (int i = 0; i < 4; ++i) {
+                const uint4 w = rraw[4 * q + i];
+                const float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), cc = unpack_bf16x2(w.z),
+                             d = unpack_bf16x2(w.w);
+                v[8 * i + 0] += a.x; v[8 * i + 1] += a.y; v[8 * i + 2] += b.x; v[8 * i + 3] += b.y;
+                v[8 * i + 4] += cc.x; v[8 * i + 5] += cc.y; v[8 * i + 6] += d.x; v[8 * i + 7] += d.y;
+              }
             }
             store_bf16x32(out + (long)m * args.ldo + n, v);
           }
@@ -489,7 +506,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!HRM_BOUNDS_OK(pos >= 0 && pos < args.rope_rows, args.err, 80)) pos = 0;
         const float4* cr = reinterpret_cast<const float4*>(args.cos_tab + (long)pos * 64 + c * 32);
         const float4* sr = reinterpret_cast<const float4*>(args.sin_tab + (long)pos * 64 + c * 32);
-#pragma unroll 1
+        // this row's 32 frequencies of the chunk, read once and used for both heads of the tile
+        const bool any_rotate = (nt * BN < args.rope_end) && (nt * BN + 256 > args.rope_begin);
+        float cs_all[32], sn_all[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 a = (row_ok && any_rotate) ? cr[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 b = (row_ok && any_rotate) ? sr[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+          cs_all[4 * q] = a.x; cs_all[4 * q + 1] = a.y; cs_all[4 * q + 2] = a.z; cs_all[4 * q + 3] = a.w;
+          sn_all[4 * q] = b.x; sn_all[4 * q + 1] = b.y; sn_all[4 * q + 2] = b.z; sn_all[4 * q + 3] = b.w;
+        }
+#pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int head_col = nt * BN + h * 128;
           const bool rotate = head_col >= args.rope_begin && head_col < args.rope_end;
@@ -498,15 +525,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             uint32_t r1[16], r2[16];
             tmem_ld_32x32b_x16(taddr + h * 128 + c * 32 + sub * 16, r1);
             tmem_ld_32x32b_x16(taddr + h * 128 + 64 + c * 32 + sub * 16, r2);
-            float cs[16], sn[16];
-            if (row_ok && rotate) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float4 a = cr[sub * 4 + q], b = sr[sub * 4 + q];
-                cs[4 * q] = a.x; cs[4 * q + 1] = a.y; cs[4 * q + 2] = a.z; cs[4 * q + 3] = a.w;
-                sn[4 * q] = b.x; sn[4 * q + 1] = b.y; sn[4 * q + 2] = b.z; sn[4 * q + 3] = b.w;
-              }
-            }
+            const float* cs = cs_all + sub * 16;
+            const float* sn = sn_all + sub * 16;
             tmem_ld_wait();
             if (row_ok && head_col < args.N) {
               uint32_t o1[8], o2[8];
@@ -556,17 +576,43 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
         __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(args.out);
-#pragma unroll 1
-        for (int c = half * 4; c < half * 4 + 4; ++c) {
+        // g / u rows of chunk c + 1 are requested while chunk c computes (one chunk of latency
+        // exposed per tile instead of four)
+        auto fetch = [&](int c, uint4 (&gr)[4], uint4 (&ur)[4]) {
           const int f = nt * BN + c * 32;
           const bool ok = row_ok && f < args.N;
-          float g[32], u[32], dh[32];
-          if (ok) {  // issue the global loads before the TMEM load to overlap their latency
-            load_bf16x32(args.aux + (long)m * args.ldaux + f, g);
-            load_bf16x32(args.aux + (long)m * args.ldaux + args.pair_offset + f, u);
+          const uint4* gs = reinterpret_cast<const uint4*>(args.aux + (long)m * args.ldaux + f);
+          const uint4* us = reinterpret_cast<const uint4*>(args.aux + (long)m * args.ldaux + args.pair_offset + f);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            gr[i] = ok ? gs[i] : make_uint4(0, 0, 0, 0);
+            ur[i] = ok ? us[i] : make_uint4(0, 0, 0, 0);
           }
+        };
+        uint4 gcur[4], ucur[4];
+        fetch(half * 4, gcur, ucur);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = half * 4 + q;
+          const int f = nt * BN + c * 32;
+          const bool ok = row_ok && f < args.N;
+          uint4 gnext[4], unext[4];
+          if (q < 3) fetch(c + 1, gnext, unext);
+          float dh[32];
           tmem_load_f32x32(taddr + c * 32, dh);
           if (ok) {
+            float g[32], u[32];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t gw[4] = {gcur[i].x, gcur[i].y, gcur[i].z, gcur[i].w};
+              const uint32_t uw[4] = {ucur[i].x, ucur[i].y, ucur[i].z, ucur[i].w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float2 a = unpack_bf16x2(gw[k]), b = unpack_bf16x2(uw[k]);
+                g[8 * i + 2 * k] = a.x; g[8 * i + 2 * k + 1] = a.y;
+                u[8 * i + 2 * k] = b.x; u[8 * i + 2 * k + 1] = b.y;
+              }
+            }
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float sg = __fdividef(1.0f, 1.0f + __expf(-g[j]));  // fast divide: outputs are bf16
@@ -578,6 +624,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
             store_bf16x32(dgu + (long)m * args.ldo + f, g);
             store_bf16x32(dgu + (long)m * args.ldo + args.pair_offset + f, u);
+          }
+          if (q < 3) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              gcur[i] = gnext[i];
+              ucur[i] = unext[i];
+            }
           }
         }
       } else if constexpr (EPI == EPI_CE_BWD) {
