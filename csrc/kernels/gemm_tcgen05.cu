@@ -60,17 +60,31 @@ constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int EPI_WARPS = 8;
 constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int GEMM_SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256;
+// bf16 outputs leave through TMA tensor stores: each epilogue warp stages a 32 x 32 box
+// (64-byte rows, 64B-swizzled) in one of its two 2 KB buffers
+// (only the epilogues with bf16 outputs reserve it: the fp32 weight-gradient GEMMs measured
+// 30-45 % slower with the extra 32 KB of shared memory they do not use)
+constexpr int STG_BOX_BYTES = 32 * 32 * 2;
+constexpr int STG_BYTES = EPI_WARPS * 2 * STG_BOX_BYTES;  // 32 KB
 template <int EPI>
-constexpr int gemm_smem_bytes() { return GEMM_SMEM_BYTES; }
+constexpr bool stages_output() {
+  return EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_ROPE || EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_BWD ||
+         EPI == EPI_CE_BWD;
+}
+template <int EPI>
+constexpr int stage_bytes() { return stages_output<EPI>() ? STG_BYTES : 0; }
+constexpr int GEMM_SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + STG_BYTES + 256;
+template <int EPI>
+constexpr int gemm_smem_bytes() { return GEMM_SMEM_BYTES - STG_BYTES + stage_bytes<EPI>(); }
 // CTA-pair (cta_group::2) variant: a 256 x 256 tile per pair of SMs, each SM stages its 128
 // rows of A and its 128 columns of B, so a k-block costs each SM 32 KB instead of 48 KB of
 // operand traffic for the same tensor-core work; 6 stages fit the same shared memory.
 constexpr int PAIR_STAGES = 6;
-constexpr int PAIR_SMEM_BYTES = 1024 + PAIR_STAGES * (A_STAGE_BYTES + B_STAGE_BYTES / 2) + 256;
+constexpr int PAIR_SMEM_BYTES = 1024 + PAIR_STAGES * (A_STAGE_BYTES + B_STAGE_BYTES / 2) + STG_BYTES + 256;
+static_assert(GEMM_SMEM_BYTES <= 232448, "GEMM exceeds the shared-memory limit");
 static_assert(PAIR_SMEM_BYTES <= 232448, "pair GEMM exceeds the shared-memory limit");
 template <int EPI>
-constexpr int pair_smem_bytes() { return PAIR_SMEM_BYTES; }
+constexpr int pair_smem_bytes() { return PAIR_SMEM_BYTES - STG_BYTES + stage_bytes<EPI>(); }
 
 struct GemmArgs {
   int M, N, K;
@@ -177,6 +191,41 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// One epilogue warp's bf16 output path: lane = row of a 32-row box, w = its 32 columns as 16
+// packed words. The box is written into one of the warp's two 2 KB buffers in the 64-byte
+// swizzle of the output tensor map (16-byte piece q of row r at (q ^ (r / 2 % 4)) * 16, which
+// keeps each quarter-warp's stores on distinct banks) and leaves with one TMA tensor store
+// issued by lane 0; rows past the tensor's end are clipped by the map. A buffer is rewritten
+// only after the store issued from it two boxes earlier has read it.
+struct OutStager {
+  uint8_t* base;
+  int k;
+  __device__ __forceinline__ void put(const CUtensorMap* map, const uint32_t (&w)[16], int lane, int x, int y) {
+    uint8_t* buf = base + k * STG_BOX_BYTES;
+    if (lane == 0) bulk_wait_read1();
+    __syncwarp();
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(buf + lane * 64 + ((q ^ sw) << 4)) =
+          make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, buf, x, y);
+      bulk_commit();
+    }
+    k ^= 1;
+  }
+};
+
+__device__ __forceinline__ void pack_bf16x32(const float (&v)[32], uint32_t (&w)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+}
 
 // Bounded spin until *flag >= value (acquire); false after the time limit.
 __device__ __forceinline__ bool wait_flag(const int* flag, int value) {
@@ -228,6 +277,7 @@ __device__ __forceinline__ void tmem_load_f32x32(uint32_t taddr, float (&v)[32])
 template <int A_MN, int B_MN, int EPI, int PAIR = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
                         const GemmArgs args) {
   constexpr int kStages = PAIR ? PAIR_STAGES : STAGES;
   constexpr int kBStage = PAIR ? B_STAGE_BYTES / 2 : B_STAGE_BYTES;
@@ -236,7 +286,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * A_STAGE_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + kStages * kBStage);
+  uint8_t* sStage = sB + kStages * kBStage;  // 1024-aligned: stage sizes are multiples of 1 KB
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sStage + stage_bytes<EPI>());
   uint64_t* empty_bar = full_bar + kStages;
   uint64_t* tfull_bar = empty_bar + kStages;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -425,6 +476,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int row = quarter * 32 + lane;
     if (args.jobs.g_src != nullptr || args.jobs.p_src != nullptr)
       run_copy_jobs(args.jobs, (int)blockIdx.x * EPI_WARPS + (warp - 2), (int)gridDim.x * EPI_WARPS, lane);
+    OutStager stg{sStage + (warp - 2) * 2 * STG_BOX_BYTES, 0};
     int local = 0;
     for_each_segment(sched, mode, split, unit, units, [&](int tile, int kb0, int kb1) -> bool {
       const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
@@ -438,6 +490,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const int m = mt * TILE_M + (int)cta_rank * BM + row;
       const bool row_ok = m < args.M;
+      const int box_y = mt * TILE_M + (int)cta_rank * BM + quarter * 32;  // this warp's 32 rows
 
       if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
@@ -459,7 +512,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           float v[32];
           tmem_load_f32x32(taddr + c * 32, v);
           const int n = nt * BN + c * 32;
-          if (row_ok && n < args.N) {
+          if (n < args.N) {  // warp-uniform; rows past M are clipped by the store
             if constexpr (EPI == EPI_RESIDUAL) {
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
@@ -470,9 +523,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 v[8 * i + 4] += cc.x; v[8 * i + 5] += cc.y; v[8 * i + 6] += d.x; v[8 * i + 7] += d.y;
               }
             }
-            store_bf16x32(out + (long)m * args.ldo + n, v);
+            uint32_t w[16];
+            pack_bf16x32(v, w);
+            stg.put(&tmC, w, lane, n, box_y);
           }
         }
+        (void)out;
       } else if constexpr (EPI == EPI_F32ADD) {
         float* out = reinterpret_cast<float*>(args.out);
         // deterministic split-K: the unit of K chunk q stores its partial into slice q (the
@@ -520,6 +576,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int h = 0; h < 2; ++h) {
           const int head_col = nt * BN + h * 128;
           const bool rotate = head_col >= args.rope_begin && head_col < args.rope_end;
+          uint32_t o1[16], o2[16];  // columns head_col + c*32 + [0,32) and head_col + 64 + c*32 + [0,32)
 #pragma unroll
           for (int sub = 0; sub < 2; ++sub) {
             uint32_t r1[16], r2[16];
@@ -528,29 +585,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const float* cs = cs_all + sub * 16;
             const float* sn = sn_all + sub * 16;
             tmem_ld_wait();
-            if (row_ok && head_col < args.N) {
-              uint32_t o1[8], o2[8];
 #pragma unroll
-              for (int j = 0; j < 16; j += 2) {
-                float a0 = __uint_as_float(r1[j]), a1 = __uint_as_float(r1[j + 1]);
-                float b0 = __uint_as_float(r2[j]), b1 = __uint_as_float(r2[j + 1]);
-                if (rotate) {
-                  const float na0 = a0 * cs[j] - b0 * sn[j], na1 = a1 * cs[j + 1] - b1 * sn[j + 1];
-                  const float nb0 = b0 * cs[j] + a0 * sn[j], nb1 = b1 * cs[j + 1] + a1 * sn[j + 1];
-                  a0 = na0; a1 = na1; b0 = nb0; b1 = nb1;
-                }
-                o1[j >> 1] = pack_bf16x2(a0, a1);
-                o2[j >> 1] = pack_bf16x2(b0, b1);
+            for (int j = 0; j < 16; j += 2) {
+              float a0 = __uint_as_float(r1[j]), a1 = __uint_as_float(r1[j + 1]);
+              float b0 = __uint_as_float(r2[j]), b1 = __uint_as_float(r2[j + 1]);
+              if (rotate) {
+                const float na0 = a0 * cs[j] - b0 * sn[j], na1 = a1 * cs[j + 1] - b1 * sn[j + 1];
+                const float nb0 = b0 * cs[j] + a0 * sn[j], nb1 = b1 * cs[j + 1] + a1 * sn[j + 1];
+                a0 = na0; a1 = na1; b0 = nb0; b1 = nb1;
               }
-              uint4* d1 = reinterpret_cast<uint4*>(out + (long)m * args.ldo + head_col + c * 32 + sub * 16);
-              uint4* d2 = reinterpret_cast<uint4*>(out + (long)m * args.ldo + head_col + 64 + c * 32 + sub * 16);
-              d1[0] = make_uint4(o1[0], o1[1], o1[2], o1[3]);
-              d1[1] = make_uint4(o1[4], o1[5], o1[6], o1[7]);
-              d2[0] = make_uint4(o2[0], o2[1], o2[2], o2[3]);
-              d2[1] = make_uint4(o2[4], o2[5], o2[6], o2[7]);
+              o1[sub * 8 + (j >> 1)] = pack_bf16x2(a0, a1);
+              o2[sub * 8 + (j >> 1)] = pack_bf16x2(b0, b1);
             }
           }
+          if (head_col < args.N) {  // warp-uniform
+            stg.put(&tmC, o1, lane, head_col + c * 32, box_y);
+            stg.put(&tmC, o2, lane, head_col + 64 + c * 32, box_y);
+          }
         }
+        (void)out;
       } else if constexpr (EPI == EPI_SWIGLU) {
         // acc columns [0,128) = gate, [128,256) = up for features nt*128 + [0,128)
         __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(args.out);
@@ -561,7 +614,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tmem_load_f32x32(taddr + c * 32, g);
           tmem_load_f32x32(taddr + 128 + c * 32, u);
           const int f = nt * 128 + c * 32;
-          if (row_ok && f < args.N) {
+          if (f < args.N) {  // warp-uniform
             float hv[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -569,13 +622,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               u[j] = bf16_round(u[j]);
               hv[j] = __fdividef(g[j], 1.0f + __expf(-g[j])) * u[j];  // fast divide: output is bf16
             }
-            store_bf16x32(gu + (long)m * args.ldo + f, g);
-            store_bf16x32(gu + (long)m * args.ldo + args.pair_offset + f, u);
-            store_bf16x32(hout + (long)m * args.ldo2 + f, hv);
+            uint32_t w[16];
+            pack_bf16x32(g, w);
+            stg.put(&tmC, w, lane, f, box_y);
+            pack_bf16x32(u, w);
+            stg.put(&tmC, w, lane, args.pair_offset + f, box_y);
+            pack_bf16x32(hv, w);
+            stg.put(&tmC2, w, lane, f, box_y);
           }
         }
+        (void)gu; (void)hout;
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
-        __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(args.out);
         // g / u rows of chunk c + 1 are requested while chunk c computes (one chunk of latency
         // exposed per tile instead of four)
         auto fetch = [&](int c, uint4 (&gr)[4], uint4 (&ur)[4]) {
@@ -595,13 +652,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int q = 0; q < 4; ++q) {
           const int c = half * 4 + q;
           const int f = nt * BN + c * 32;
-          const bool ok = row_ok && f < args.N;
           uint4 gnext[4], unext[4];
           if (q < 3) fetch(c + 1, gnext, unext);
           float dh[32];
           tmem_load_f32x32(taddr + c * 32, dh);
-          if (ok) {
-            float g[32], u[32];
+          float g[32], u[32];  // rows past M hold zeros from fetch; their stores are clipped
+          {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint32_t gw[4] = {gcur[i].x, gcur[i].y, gcur[i].z, gcur[i].w};
@@ -622,8 +678,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               g[j] = d * u[j] * dsilu;
               u[j] = d * silu;
             }
-            store_bf16x32(dgu + (long)m * args.ldo + f, g);
-            store_bf16x32(dgu + (long)m * args.ldo + args.pair_offset + f, u);
+          }
+          if (f < args.N) {  // warp-uniform; rows past M are clipped by the store
+            uint32_t w[16];
+            pack_bf16x32(g, w);
+            stg.put(&tmC, w, lane, f, box_y);
+            pack_bf16x32(u, w);
+            stg.put(&tmC, w, lane, args.pair_offset + f, box_y);
           }
           if (q < 3) {
 #pragma unroll
@@ -647,15 +708,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           float v[32];
           tmem_load_f32x32(taddr + c * 32, v);
           const int n = nt * BN + c * 32;
-          if (row_ok && n < args.N) {
+          if (n < args.N) {  // warp-uniform; rows past M are clipped by the store
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float prob = __expf(bf16_round(v[j]) - lse);
               v[j] = label < 0 ? 0.f : (prob - (col0 + n + j == label ? 1.f : 0.f)) * g;
             }
-            store_bf16x32(out + (long)m * args.ldo + n, v);
+            uint32_t w[16];
+            pack_bf16x32(v, w);
+            stg.put(&tmC, w, lane, n, box_y);
           }
         }
+        (void)out;
       } else if constexpr (EPI == EPI_CE) {
         // Partial softmax statistics over this warp's 128 columns; partial index nt*2 + half.
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
@@ -709,6 +773,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     });
   }
 
+  if (warp >= 2 && lane == 0) bulk_wait0();  // this warp's output stores are complete
   tc_fence_before();
   __syncthreads();
   // pairs: the leader's UMMAs write the peer's TMEM and read its shared memory, and its commits
@@ -764,6 +829,24 @@ CUtensorMap make_map(const at::Tensor& t, int64_t inner, int64_t outer, int64_t 
   return map;
 }
 
+// bf16 output tensor [rows, t.size(1)] (row stride t.stride(0)) as 32 x 32 boxes in the 64-byte
+// swizzle that OutStager writes.
+CUtensorMap make_out_map(const at::Tensor& t, int64_t rows) {
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1, "GEMM output must be row-major bf16");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0 && (t.stride(0) * 2) % 16 == 0,
+              "GEMM output base and row stride must be 16-byte aligned");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)t.size(1), (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(t.stride(0) * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (output) failed with code ", (int)r);
+  return map;
+}
+
 int num_sms() { return device_sm_count(); }
 
 // CTA pairs that can be resident at once (cluster placement can leave SMs unused).
@@ -798,8 +881,8 @@ int max_pair_clusters() {
 }
 
 template <int A_MN, int B_MN, int EPI>
-void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int clusters,
-                 cudaStream_t stream) {
+void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mc2,
+                 const GemmArgs& args, int clusters, cudaStream_t stream) {
   auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, 1>;
   max_pair_clusters<A_MN, B_MN, EPI>();  // sets the shared-memory attribute
   cudaLaunchConfig_t cfg = {};
@@ -814,16 +897,17 @@ void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, args) == cudaSuccess, "pair GEMM launch failed");
+  TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mc2, args) == cudaSuccess, "pair GEMM launch failed");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <int A_MN, int B_MN, int EPI>
-void launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int grid, cudaStream_t stream) {
+void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mc2,
+            const GemmArgs& args, int grid, cudaStream_t stream) {
   auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI>;
   TORCH_CHECK(ensure_dynamic_smem((const void*)kern, gemm_smem_bytes<EPI>()) == cudaSuccess,
               "cudaFuncSetAttribute failed");
-  kern<<<grid, GEMM_THREADS, gemm_smem_bytes<EPI>(), stream>>>(ma, mb, args);
+  kern<<<grid, GEMM_THREADS, gemm_smem_bytes<EPI>(), stream>>>(ma, mb, mc, mc2, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -908,6 +992,16 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   CUtensorMap ma = a_mn ? make_map(a, M, K, a.stride(0), 64, 64) : make_map(a, K, M, a.stride(0), 64, 128);
   const int64_t b_rows = b_mn ? K : b.size(0);
   CUtensorMap mb = b_mn ? make_map(b, N, K, b.stride(0), 64, 64) : make_map(b, K, b_rows, b.stride(0), 64, 128);
+  // bf16 outputs leave through TMA stores (OutStager); other epilogues get unused placeholders
+  CUtensorMap mc = ma, mc2 = ma;
+  if (epi == EPI_STORE || epi == EPI_RESIDUAL || epi == EPI_ROPE || epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD ||
+      epi == EPI_CE_BWD) {
+    mc = make_out_map(out, M);
+    if (epi == EPI_SWIGLU) {
+      TORCH_CHECK(out2.has_value(), "gemm: the SwiGLU epilogue needs its second output");
+      mc2 = make_out_map(*out2, M);
+    }
+  }
 
   const int64_t n_tiles = (epi == EPI_SWIGLU) ? (N + 127) / 128 : (N + BN - 1) / BN;
   // CTA pairs (256-row tiles) unless the problem is too short to fill them
@@ -922,7 +1016,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   if (a_mn == AM && b_mn == BMJ && epi == E) {                                                     \
     const int cl = max_pair_clusters<AM, BMJ, E>();                                                \
     const int clusters = (E == EPI_F32ADD && stream_k) ? cl : (int)std::min<int64_t>(tiles, cl);   \
-    return launch_pair<AM, BMJ, E>(ma, mb, args, clusters, stream);                                \
+    return launch_pair<AM, BMJ, E>(ma, mb, mc, mc2, args, clusters, stream);                      \
   }
     HRM_GEMM_PAIR_CASE(0, 0, EPI_STORE)
     HRM_GEMM_PAIR_CASE(0, 0, EPI_RESIDUAL)
@@ -945,7 +1039,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   if (epi == EPI_F32ADD && stream_k) grid = num_sms();
 
 #define HRM_GEMM_CASE(AM, BMJ, E) \
-  if (a_mn == AM && b_mn == BMJ && epi == E) return launch<AM, BMJ, E>(ma, mb, args, grid, stream);
+  if (a_mn == AM && b_mn == BMJ && epi == E) return launch<AM, BMJ, E>(ma, mb, mc, mc2, args, grid, stream);
   HRM_GEMM_CASE(0, 0, EPI_STORE)
   HRM_GEMM_CASE(0, 0, EPI_RESIDUAL)
   HRM_GEMM_CASE(0, 0, EPI_ROPE)
