@@ -229,6 +229,34 @@ __global__ void adam_atan2_kernel(float* __restrict__ p, const float* __restrict
   }
 }
 
+// Same update, four parameters per thread with 16-byte loads / stores (all buffers 16-byte
+// aligned, n a multiple of 4): the optimizer moves ~38 bytes per parameter, so it is bound by
+// HBM bandwidth and the scalar version left a third of it unused.
+__global__ void adam_atan2_vec4_kernel(float4* __restrict__ p, const float4* __restrict__ g, float4* __restrict__ m,
+                                       float4* __restrict__ v, float4* __restrict__ ema, uint2* __restrict__ out16,
+                                       long n4, const float* __restrict__ hyper, float beta1, float beta2, float wd,
+                                       float ema_decay) {
+  const float lr = hyper[0], inv_bc1 = hyper[1], inv_bc2_sqrt = hyper[2];
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    float4 pv = p[i], gv = g[i], vv = v[i];
+    float4 mv = m != nullptr ? m[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    float* pp = &pv.x; const float* gg = &gv.x; float* vp = &vv.x; float* mp = &mv.x;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      pp[e] = adam_atan2_update(pp[e], gg[e], m != nullptr, mp[e], vp[e], lr, inv_bc1, inv_bc2_sqrt, beta1, beta2, wd);
+    p[i] = pv;
+    v[i] = vv;
+    if (m != nullptr) m[i] = mv;
+    if (ema != nullptr) {
+      float4 e = ema[i];
+      const float d = 1.f - ema_decay;
+      e.x += d * (pv.x - e.x); e.y += d * (pv.y - e.y); e.z += d * (pv.z - e.z); e.w += d * (pv.w - e.w);
+      ema[i] = e;
+    }
+    if (out16 != nullptr) out16[i] = make_uint2(pack_bf16x2(pv.x, pv.y), pack_bf16x2(pv.z, pv.w));
+  }
+}
+
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long n) {
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
     dst[i] = __float2bfloat16(src[i]);
@@ -338,6 +366,20 @@ void adam_atan2(const at::Tensor& p, const at::Tensor& g, const c10::optional<at
   c10::cuda::CUDAGuard guard(p.device());
   const long n = p.numel();
   TORCH_CHECK(g.numel() == n && v.numel() == n, "adam_atan2: size mismatch");
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const bool vec = n % 4 == 0 && a16(p.data_ptr()) && a16(g.data_ptr()) && a16(v.data_ptr()) &&
+                   (!m || a16(m->data_ptr())) && (!ema || a16(ema->data_ptr())) &&
+                   (!out16 || (reinterpret_cast<uintptr_t>(out16->data_ptr()) & 7) == 0);
+  if (vec) {
+    adam_atan2_vec4_kernel<<<grid_for(n / 4, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<float4*>(p.data_ptr<float>()), reinterpret_cast<const float4*>(g.data_ptr<float>()),
+        m ? reinterpret_cast<float4*>(m->data_ptr<float>()) : nullptr, reinterpret_cast<float4*>(v.data_ptr<float>()),
+        ema ? reinterpret_cast<float4*>(ema->data_ptr<float>()) : nullptr,
+        out16 ? reinterpret_cast<uint2*>(out16->data_ptr()) : nullptr, n / 4, hyper.data_ptr<float>(), (float)beta1,
+        (float)beta2, (float)wd, (float)ema_decay);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   adam_atan2_kernel<<<grid_for(n, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       p.data_ptr<float>(), g.data_ptr<float>(), m ? m->data_ptr<float>() : nullptr, v.data_ptr<float>(),
       ema ? ema->data_ptr<float>() : nullptr, out16 ? bfm(*out16) : nullptr, n, hyper.data_ptr<float>(),
