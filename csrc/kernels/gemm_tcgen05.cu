@@ -849,6 +849,23 @@ CUtensorMap make_out_map(const at::Tensor& t, int64_t rows) {
 
 int num_sms() { return device_sm_count(); }
 
+// Split-K factor of an fp32 weight-gradient GEMM: at least `s0` (the split whose K-chunk operand
+// panels stay L2-sized), up to 2*s0 + 2, minimising the estimated time of `tiles * s` units on
+// `units` persistent CTA pairs: waves * (1/s + c), where c = 0.05 of a whole tile's main loop is
+// the per-unit cost (epilogue, fp32 reductions, pipeline fill; fitted on the HRM-Text L weight
+// gradients). It changes only GEMMs whose units quantise badly: the L o_proj gradient
+// (25 tiles x 3 units on 74 pairs: two waves for one wave's work) went from 0.107 to 0.064 ms.
+int balanced_split(int s0, int64_t tiles, int units, int64_t nk) {
+  if (s0 <= 1 || units <= 0) return s0;
+  auto cost = [&](int s) { return (double)((tiles * s + units - 1) / units) * (1.0 / s + 0.05); };
+  const int hi = (int)std::min<int64_t>(2 * s0 + 2, nk);
+  double best = cost(s0);
+  for (int s = s0 + 1; s <= hi; ++s) best = std::min(best, cost(s));
+  for (int s = s0; s <= hi; ++s)
+    if (cost(s) <= best * 1.02) return s;
+  return s0;
+}
+
 // CTA pairs that can be resident at once (cluster placement can leave SMs unused).
 template <int A_MN, int B_MN, int EPI>
 int max_pair_clusters() {
@@ -979,7 +996,13 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   args.splitk = 1;
   if (epi == EPI_F32ADD && stream_k) {
     const double panel_bytes = 2.0 * (double)K * (double)(M + N);
-    args.splitk = (int)std::min<double>(16.0, std::max(1.0, std::ceil(panel_bytes / (48.0 * 1024 * 1024))));
+    // operand bytes per K chunk, HRM_WGRAD_PANEL_MB (default 72 MB: at L, 48 / 72 / 96 MB measured
+    // gate/up 0.373 / 0.315 / 0.309 ms, qkv 0.231 / 0.224 / 0.229 ms, down 0.156 / 0.151 / 0.151)
+    static const double panel_target = [] {
+      const char* v = std::getenv("HRM_WGRAD_PANEL_MB");
+      return (v != nullptr && std::atof(v) > 0.0) ? std::atof(v) * 1024.0 * 1024.0 : 72.0 * 1024.0 * 1024.0;
+    }();
+    args.splitk = (int)std::min<double>(16.0, std::max(1.0, std::ceil(panel_bytes / panel_target)));
     static const bool chunked = [] {
       const char* v = std::getenv("HRM_WGRAD_SPLITK");
       return v == nullptr || std::string(v) != "0";
@@ -1012,6 +1035,12 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   const bool pair = pair_enabled && M >= 1024;
   if (pair) {
     const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * n_tiles;
+    static const bool balance = [] {  // HRM_WGRAD_BALANCE=0: the plain L2-sized split (A/B runs)
+      const char* v = std::getenv("HRM_WGRAD_BALANCE");
+      return v == nullptr || std::string(v) != "0";
+    }();
+    if (balance && epi == EPI_F32ADD && stream_k && splitk <= 0 && args.splitk > 1)  // automatic split only
+      args.splitk = balanced_split(args.splitk, tiles, max_pair_clusters<1, 1, EPI_F32ADD>(), (K + BK - 1) / BK);
 #define HRM_GEMM_PAIR_CASE(AM, BMJ, E)                                                             \
   if (a_mn == AM && b_mn == BMJ && epi == E) {                                                     \
     const int cl = max_pair_clusters<AM, BMJ, E>();                                                \

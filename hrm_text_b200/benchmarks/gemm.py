@@ -45,6 +45,8 @@ def main(argv=None):
     dy_qkv = rnd(T, 4 * h, scale=0.01)
     grad_qkv = torch.zeros(4 * h, h, device=dev)
     grad_d = torch.zeros(h, inter, device=dev)
+    grad_gu = torch.zeros(2 * inter, h, device=dev)
+    grad_o = torch.zeros(h, h, device=dev)
     vocab = 32768
     w_head = rnd(vocab, h, scale=0.02)
     labels = torch.randint(0, vocab, (T,), device=dev, dtype=torch.int32)
@@ -57,6 +59,8 @@ def main(argv=None):
         "qkv_dgrad": (lambda: G.linear_dgrad(dy_qkv, w_qkv), 2 * T * 4 * h * h),
         "qkv_wgrad": (lambda: G.linear_wgrad_(dy_qkv, x, grad_qkv), 2 * T * 4 * h * h),
         "down_wgrad": (lambda: G.linear_wgrad_(dy_h, hmid, grad_d), 2 * T * h * inter),
+        "gate_up_wgrad": (lambda: G.linear_wgrad_(gu, x, grad_gu), 2 * T * 2 * inter * h),
+        "o_wgrad": (lambda: G.linear_wgrad_(dy_h, x, grad_o), 2 * T * h * h),
         "lm_head_ce": (lambda: G.lm_head_ce_stats(x, w_head, labels), 2 * T * vocab * h),
     }
     results = {}
