@@ -71,20 +71,29 @@ constexpr bool stages_output() {
   return EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_ROPE || EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_BWD ||
          EPI == EPI_CE_BWD;
 }
+// The SwiGLU backward also brings its g / u inputs in through TMA: each warp holds two
+// (g | u) box pairs (8 KB), and the main loop keeps fewer stages to make room (K is the hidden
+// size, 20 k-blocks at L).
 template <int EPI>
-constexpr int stage_bytes() { return stages_output<EPI>() ? STG_BYTES : 0; }
-constexpr int GEMM_SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + STG_BYTES + 256;
+constexpr int stage_bytes() { return EPI == EPI_SWIGLU_BWD ? 2 * STG_BYTES : stages_output<EPI>() ? STG_BYTES : 0; }
 template <int EPI>
-constexpr int gemm_smem_bytes() { return GEMM_SMEM_BYTES - STG_BYTES + stage_bytes<EPI>(); }
+constexpr int single_stages() { return EPI == EPI_SWIGLU_BWD ? 3 : STAGES; }
+template <int EPI>
+constexpr int pair_stages() { return EPI == EPI_SWIGLU_BWD ? 4 : 6; }
+constexpr int BAR_BYTES = 512;  // mbarriers + TMEM slot
+template <int EPI>
+constexpr int gemm_smem_bytes() {
+  return 1024 + single_stages<EPI>() * (A_STAGE_BYTES + B_STAGE_BYTES) + stage_bytes<EPI>() + BAR_BYTES;
+}
+static_assert(gemm_smem_bytes<0>() <= 232448 && gemm_smem_bytes<5>() <= 232448, "GEMM exceeds shared memory");
 // CTA-pair (cta_group::2) variant: a 256 x 256 tile per pair of SMs, each SM stages its 128
 // rows of A and its 128 columns of B, so a k-block costs each SM 32 KB instead of 48 KB of
 // operand traffic for the same tensor-core work; 6 stages fit the same shared memory.
-constexpr int PAIR_STAGES = 6;
-constexpr int PAIR_SMEM_BYTES = 1024 + PAIR_STAGES * (A_STAGE_BYTES + B_STAGE_BYTES / 2) + STG_BYTES + 256;
-static_assert(GEMM_SMEM_BYTES <= 232448, "GEMM exceeds the shared-memory limit");
-static_assert(PAIR_SMEM_BYTES <= 232448, "pair GEMM exceeds the shared-memory limit");
 template <int EPI>
-constexpr int pair_smem_bytes() { return PAIR_SMEM_BYTES - STG_BYTES + stage_bytes<EPI>(); }
+constexpr int pair_smem_bytes() {
+  return 1024 + pair_stages<EPI>() * (A_STAGE_BYTES + B_STAGE_BYTES / 2) + stage_bytes<EPI>() + BAR_BYTES;
+}
+static_assert(pair_smem_bytes<0>() <= 232448 && pair_smem_bytes<5>() <= 232448, "pair GEMM exceeds shared memory");
 
 struct GemmArgs {
   int M, N, K;
@@ -279,7 +288,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
                         const GemmArgs args) {
-  constexpr int kStages = PAIR ? PAIR_STAGES : STAGES;
+  constexpr int kStages = PAIR ? pair_stages<EPI>() : single_stages<EPI>();
   constexpr int kBStage = PAIR ? B_STAGE_BYTES / 2 : B_STAGE_BYTES;
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
   extern __shared__ uint8_t smem_raw[];
@@ -292,7 +301,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* tfull_bar = empty_bar + kStages;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* aux_bar = drain_bar + 1;  // SwiGLU backward: [epilogue warp][box pair] input loads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 2 * EPI_WARPS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -321,6 +331,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&tempty_bar[a], PAIR ? 2 * EPI_WARPS : 32 * EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < 2 * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -477,6 +488,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (args.jobs.g_src != nullptr || args.jobs.p_src != nullptr)
       run_copy_jobs(args.jobs, (int)blockIdx.x * EPI_WARPS + (warp - 2), (int)gridDim.x * EPI_WARPS, lane);
     OutStager stg{sStage + (warp - 2) * 2 * STG_BOX_BYTES, 0};
+    // SwiGLU backward: this warp's two (g | u) box pairs, and the chunk stream they are loaded for
+    uint8_t* aux_base = sStage + (warp - 2) * 4 * STG_BOX_BYTES;
+    uint64_t* my_aux_bar = aux_bar + 2 * (warp - 2);
+    int aux_j = 0;           // chunks of this warp consumed so far (pair = j & 1, phase = (j >> 1) & 1)
+    int aux_loaded = 0;      // chunks whose loads were issued
+    // lane 0: g and u boxes of chunk (mt, nt, c) into pair p
+    auto aux_issue = [&](int p, int lmt, int lnt, int c) {
+      if (lane == 0) {
+        uint8_t* b = aux_base + p * 2 * STG_BOX_BYTES;
+        const int y = lmt * TILE_M + (int)cta_rank * BM + quarter * 32;
+        const int f = lnt * BN + c * 32;
+        mbar_arrive_expect_tx(&my_aux_bar[p], 2 * STG_BOX_BYTES);
+        tma_load_2d(b, &tmC2, &my_aux_bar[p], f, y);
+        tma_load_2d(b + STG_BOX_BYTES, &tmC2, &my_aux_bar[p], args.pair_offset + f, y);
+      }
+    };
     int local = 0;
     for_each_segment(sched, mode, split, unit, units, [&](int tile, int kb0, int kb1) -> bool {
       const int mt = tile / sched.n_tiles, nt = tile % sched.n_tiles;
@@ -633,66 +660,76 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         (void)gu; (void)hout;
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
-        // g / u rows of chunk c + 1 are requested while chunk c computes (one chunk of latency
-        // exposed per tile instead of four)
-        auto fetch = [&](int c, uint4 (&gr)[4], uint4 (&ur)[4]) {
-          const int f = nt * BN + c * 32;
-          const bool ok = row_ok && f < args.N;
-          const uint4* gs = reinterpret_cast<const uint4*>(args.aux + (long)m * args.ldaux + f);
-          const uint4* us = reinterpret_cast<const uint4*>(args.aux + (long)m * args.ldaux + args.pair_offset + f);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            gr[i] = ok ? gs[i] : make_uint4(0, 0, 0, 0);
-            ur[i] = ok ? us[i] : make_uint4(0, 0, 0, 0);
-          }
-        };
-        uint4 gcur[4], ucur[4];
-        fetch(half * 4, gcur, ucur);
-#pragma unroll
+        // g / u arrive as 32 x 32 TMA boxes in this warp's buffers (loads for the next chunk,
+        // also across tiles, are issued before this chunk is computed); d(gate) / d(up) are
+        // written over them in place and leave through TMA stores. Rows past M load as zeros
+        // and their stores are clipped.
+        const int next_tile = tile + units;  // whole-tile schedule: this warp's next tile
+        if (aux_loaded == aux_j) {           // nothing in flight (first tile of the warp)
+          aux_issue(aux_j & 1, mt, nt, half * 4);
+          ++aux_loaded;
+        }
+#pragma unroll 1
         for (int q = 0; q < 4; ++q) {
           const int c = half * 4 + q;
           const int f = nt * BN + c * 32;
-          uint4 gnext[4], unext[4];
-          if (q < 3) fetch(c + 1, gnext, unext);
+          const int p = aux_j & 1;
+          // the other pair held the previous chunk: its stores must have read it before reuse
+          const bool more = q < 3 || next_tile < sched.tiles();
+          if (more) {
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+            const int nq = q < 3 ? q + 1 : 0;
+            const int nmt = q < 3 ? mt : next_tile / sched.n_tiles, nnt = q < 3 ? nt : next_tile % sched.n_tiles;
+            aux_issue(p ^ 1, nmt, nnt, half * 4 + nq);
+            ++aux_loaded;
+          }
           float dh[32];
           tmem_load_f32x32(taddr + c * 32, dh);
-          float g[32], u[32];  // rows past M hold zeros from fetch; their stores are clipped
-          {
+          if (!__all_sync(0xffffffffu, mbar_wait(&my_aux_bar[p], (aux_j >> 1) & 1))) {
+            report_error(args.err, kErrGemmWaitTimeout, 6);
+            return false;
+          }
+          uint8_t* gb = aux_base + p * 2 * STG_BOX_BYTES;
+          uint8_t* ub = gb + STG_BOX_BYTES;
+          const int sw = (lane >> 1) & 3;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint32_t gw[4] = {gcur[i].x, gcur[i].y, gcur[i].z, gcur[i].w};
-              const uint32_t uw[4] = {ucur[i].x, ucur[i].y, ucur[i].z, ucur[i].w};
+          for (int i = 0; i < 4; ++i) {
+            uint4* gp = reinterpret_cast<uint4*>(gb + lane * 64 + ((i ^ sw) << 4));
+            uint4* up = reinterpret_cast<uint4*>(ub + lane * 64 + ((i ^ sw) << 4));
+            const uint4 gw4 = *gp, uw4 = *up;
+            const uint32_t gw[4] = {gw4.x, gw4.y, gw4.z, gw4.w};
+            const uint32_t uw[4] = {uw4.x, uw4.y, uw4.z, uw4.w};
+            uint32_t dgw[4], duw[4];
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float2 a = unpack_bf16x2(gw[k]), b = unpack_bf16x2(uw[k]);
-                g[8 * i + 2 * k] = a.x; g[8 * i + 2 * k + 1] = a.y;
-                u[8 * i + 2 * k] = b.x; u[8 * i + 2 * k + 1] = b.y;
+            for (int k = 0; k < 4; ++k) {
+              const float2 g2 = unpack_bf16x2(gw[k]), u2 = unpack_bf16x2(uw[k]);
+              float o_g[2], o_u[2];
+              const float gv[2] = {g2.x, g2.y}, uv[2] = {u2.x, u2.y};
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float sg = __fdividef(1.0f, 1.0f + __expf(-gv[e]));  // fast divide: outputs are bf16
+                const float silu = gv[e] * sg;
+                const float dsilu = sg * (1.0f + gv[e] * (1.0f - sg));
+                const float d = bf16_round(dh[8 * i + 2 * k + e]);
+                o_g[e] = d * uv[e] * dsilu;
+                o_u[e] = d * silu;
               }
+              dgw[k] = pack_bf16x2(o_g[0], o_g[1]);
+              duw[k] = pack_bf16x2(o_u[0], o_u[1]);
             }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float sg = __fdividef(1.0f, 1.0f + __expf(-g[j]));  // fast divide: outputs are bf16
-              const float silu = g[j] * sg;
-              const float dsilu = sg * (1.0f + g[j] * (1.0f - sg));
-              const float d = bf16_round(dh[j]);
-              g[j] = d * u[j] * dsilu;
-              u[j] = d * silu;
-            }
+            *gp = make_uint4(dgw[0], dgw[1], dgw[2], dgw[3]);
+            *up = make_uint4(duw[0], duw[1], duw[2], duw[3]);
           }
-          if (f < args.N) {  // warp-uniform; rows past M are clipped by the store
-            uint32_t w[16];
-            pack_bf16x32(g, w);
-            stg.put(&tmC, w, lane, f, box_y);
-            pack_bf16x32(u, w);
-            stg.put(&tmC, w, lane, args.pair_offset + f, box_y);
+          fence_async_smem();
+          __syncwarp();
+          if (f < args.N && lane == 0) {  // warp-uniform column bound
+            const int y = mt * TILE_M + (int)cta_rank * BM + quarter * 32;
+            tma_store_2d(&tmC, gb, f, y);
+            tma_store_2d(&tmC, ub, args.pair_offset + f, y);
           }
-          if (q < 3) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              gcur[i] = gnext[i];
-              ucur[i] = unext[i];
-            }
-          }
+          if (lane == 0) bulk_commit();
+          ++aux_j;
         }
       } else if constexpr (EPI == EPI_CE_BWD) {
         // Logits of one V chunk (columns [col0, col0 + N) of the head), recomputed by this GEMM
@@ -771,6 +808,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       ++local;
       return true;
     });
+    if constexpr (EPI == EPI_SWIGLU_BWD) {
+      // loads issued for chunks that were never consumed (a wait gave up): let them land
+      for (int jj = aux_j; jj < aux_loaded; ++jj) mbar_wait(&my_aux_bar[jj & 1], (jj >> 1) & 1);
+    }
   }
 
   if (warp >= 2 && lane == 0) bulk_wait0();  // this warp's output stores are complete
@@ -1023,6 +1064,10 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
     if (epi == EPI_SWIGLU) {
       TORCH_CHECK(out2.has_value(), "gemm: the SwiGLU epilogue needs its second output");
       mc2 = make_out_map(*out2, M);
+    }
+    if (epi == EPI_SWIGLU_BWD) {  // g | u inputs, loaded as boxes of the same shape
+      TORCH_CHECK(aux.has_value() && aux->size(1) >= 2 * pair_offset, "gemm: the SwiGLU backward needs g | u");
+      mc2 = make_out_map(*aux, M);
     }
   }
 
