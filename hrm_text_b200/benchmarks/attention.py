@@ -43,6 +43,8 @@ def main(argv=None):
     ap.add_argument("--only", default="both", choices=["fwd", "bwd", "both"])
     ap.add_argument("--phases", action="store_true", help="trace the backward's per-phase cycles (tcgen05)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--noalloc", action="store_true",
+                    help="also time the allocation-free C entry point (schedule build + forward per call)")
     args = ap.parse_args(argv)
 
     from ..data.synthetic import packed_batches
@@ -83,6 +85,8 @@ def main(argv=None):
         ms = timed(lambda: attention_fwd(qkv, H, sched, kernel=args.kernel))
         out["fwd_ms"] = ms
         out["fwd_tflops"] = fwd_flop / ms / 1e9
+    if args.noalloc:
+        out.update(_noalloc_times(qkv, H, packed, timed, fwd_flop, o, y, lse))
     if args.only in ("bwd", "both"):
         dy = torch.randn(T, H * 128, device=dev).bfloat16()
         ms = timed(lambda: attention_bwd(qkv, H, sched, o, lse, dy, packed.position_ids, cos, sin))
@@ -96,6 +100,36 @@ def main(argv=None):
     from ..utils.errors import check_device_errors
     check_device_errors()
     print(json.dumps(out))
+
+
+def _noalloc_times(qkv, H, packed, timed, fwd_flop, o, y, lse) -> dict:
+    """``hrm_attn_fwd_noalloc`` through its exported C symbol, with the regular forward's schedule
+    build included in the comparison (the entry point builds its schedule in every call)."""
+    import ctypes
+
+    import hrm_text_b200._C as ext
+    from ..ops.attention import PackedSeq, attention_fwd
+    lib = ctypes.CDLL(ext.__file__)
+    fn = lib.hrm_attn_fwd_noalloc
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                   ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
+                   ctypes.c_void_p, ctypes.c_void_p]
+    T = qkv.shape[0]
+    cu, pl = packed.cu_seqlens.to(torch.int32).contiguous(), packed.prefix_lens.to(torch.int32).contiguous()
+    out, yy, ll = torch.empty_like(o), torch.empty_like(y), torch.empty_like(lse)
+
+    def call():
+        rc = fn(qkv.data_ptr(), qkv.stride(0), T, H, cu.data_ptr(), cu.numel(), pl.data_ptr(), 0, out.data_ptr(),
+                yy.data_ptr(), out.stride(0), ll.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"hrm_attn_fwd_noalloc returned {rc}")
+
+    ms = timed(call)
+    ms_reg = timed(lambda: attention_fwd(qkv, H, PackedSeq(packed.position_ids, packed.cu_seqlens,
+                                                            packed.prefix_lens).schedule(False)))
+    return {"noalloc_fwd_ms": ms, "noalloc_fwd_tflops": fwd_flop / ms / 1e9,
+            "regular_fwd_with_schedule_ms": ms_reg}
 
 
 def _reference_times(qkv, H, b, s, dev, timed, fwd_flop, only) -> dict:
