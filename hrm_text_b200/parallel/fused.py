@@ -106,10 +106,8 @@ class FusedCollectives:
         self.buf16.zero_()
         self.base32 = torch.tensor(list(self.handle32.buffer_ptrs), dtype=torch.int64, device=dev)
 
-        self.base32_list = [int(b) for b in self.handle32.buffer_ptrs]
         # local per-step flags: one per F2 weight, set by its push job (one memset per step)
         self.local_counts = torch.zeros(max(1, len(f2_slots)), dtype=torch.int32, device=dev)
-        self._f1_slots, self._f2_slots = f1_slots, f2_slots
         self.f1: dict[str, F1Info] = {}
         self.f2: dict[str, F2Info] = {}
         cnt = self.cnt_off
