@@ -23,7 +23,7 @@ def test_hrm_l_linear_flops_per_token():
     per_token = step_flops(m, batch, {"bp_steps": 5}) / T
     stack = sum(p.numel() for p in m.model.L_level.parameters())
     assert per_token == (8 * 2 + 5 * 4) * stack + 6 * 32768 * 1280
-    assert abs(per_token / 1e9 - 9.7) < 0.1  # the survey's 9.7 GF/token for L at bp=5
+    assert abs(per_token / 1e9 - 9.7) < 0.1  # 9.7 GF of linear-layer work per token for L at bp_steps = 5
 
 
 def test_meter_reports_on_cpu():
