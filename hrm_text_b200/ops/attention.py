@@ -64,7 +64,7 @@ def attention_fwd(gqkv: Tensor, num_heads: int, sched: Tensor, kernel: str = "tc
 
     ``kernel="tcgen05"`` (training path) runs the TMEM/UMMA kernel (attention_tc.cu);
     ``kernel="mma"`` runs the warp-level mma.sync kernel (attention.cu), kept as a
-    cross-check and as the kernel behind the allocation-free C entry point.
+    cross-check.
     """
     T = gqkv.shape[0]
     width = num_heads * 128
