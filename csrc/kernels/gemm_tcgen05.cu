@@ -520,20 +520,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const bool row_ok = m < args.M;
       const int box_y = mt * TILE_M + (int)cta_rank * BM + quarter * 32;  // this warp's 32 rows
 
-      if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-        // residual: all four chunks' rows are requested before the first TMEM load, so their
-        // latency overlaps instead of being paid once per chunk
-        uint4 rraw[EPI == EPI_RESIDUAL ? 16 : 1];
-        if constexpr (EPI == EPI_RESIDUAL) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int n = nt * BN + (half * 4 + q) * 32;
-            const uint4* src = reinterpret_cast<const uint4*>(args.residual + (long)m * args.ldr + n);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) rraw[4 * q + i] = (row_ok && n < args.N) ? src[i] : make_uint4(0, 0, 0, 0);
-          }
-        }
+      if constexpr (EPI == EPI_STORE) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int c = half * 4 + q;
@@ -541,22 +528,66 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tmem_load_f32x32(taddr + c * 32, v);
           const int n = nt * BN + c * 32;
           if (n < args.N) {  // warp-uniform; rows past M are clipped by the store
-            if constexpr (EPI == EPI_RESIDUAL) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const uint4 w = rraw[4 * q + i];
-                const float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), cc = unpack_bf16x2(w.z),
-                             d = unpack_bf16x2(w.w);
-                v[8 * i + 0] += a.x; v[8 * i + 1] += a.y; v[8 * i + 2] += b.x; v[8 * i + 3] += b.y;
-                v[8 * i + 4] += cc.x; v[8 * i + 5] += cc.y; v[8 * i + 6] += d.x; v[8 * i + 7] += d.y;
-              }
-            }
             uint32_t w[16];
             pack_bf16x32(v, w);
             stg.put(&tmC, w, lane, n, box_y);
           }
         }
-        (void)out;
+      } else if constexpr (EPI == EPI_RESIDUAL) {
+        // The residual arrives as 32 x 32 TMA boxes in this warp's two buffers (the next chunk's
+        // load, also across tiles, is issued before this chunk is computed); the sum is written
+        // over it in place and leaves through a TMA store. Rows past M load as zeros and their
+        // stores are clipped; the output may alias the residual (each box is read, then written).
+        uint8_t* res_base = sStage + (warp - 2) * 2 * STG_BOX_BYTES;
+        auto res_issue = [&](int p, int lmt, int lnt, int c) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&my_aux_bar[p], STG_BOX_BYTES);
+            tma_load_2d(res_base + p * STG_BOX_BYTES, &tmC2, &my_aux_bar[p], lnt * BN + c * 32,
+                        lmt * TILE_M + (int)cta_rank * BM + quarter * 32);
+          }
+        };
+        const int next_tile = tile + units;  // whole-tile schedule: this warp's next tile
+        if (aux_loaded == aux_j) {           // nothing in flight (first tile of the warp)
+          res_issue(aux_j & 1, mt, nt, half * 4);
+          ++aux_loaded;
+        }
+#pragma unroll 1
+        for (int q = 0; q < 4; ++q) {
+          const int c = half * 4 + q;
+          const int n = nt * BN + c * 32;
+          const int p = aux_j & 1;
+          if (q < 3 || next_tile < sched.tiles()) {
+            if (lane == 0) bulk_wait_read0();  // the previous chunk's store has read the other buffer
+            __syncwarp();
+            const int nmt = q < 3 ? mt : next_tile / sched.n_tiles, nnt = q < 3 ? nt : next_tile % sched.n_tiles;
+            res_issue(p ^ 1, nmt, nnt, q < 3 ? c + 1 : half * 4);
+            ++aux_loaded;
+          }
+          float v[32];
+          tmem_load_f32x32(taddr + c * 32, v);
+          if (!__all_sync(0xffffffffu, mbar_wait(&my_aux_bar[p], (aux_j >> 1) & 1))) {
+            report_error(args.err, kErrGemmWaitTimeout, 7);
+            return false;
+          }
+          uint8_t* rb = res_base + p * STG_BOX_BYTES;
+          const int sw = (lane >> 1) & 3;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4* rp = reinterpret_cast<uint4*>(rb + lane * 64 + ((i ^ sw) << 4));
+            const uint4 w = *rp;
+            const float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), cc = unpack_bf16x2(w.z),
+                         d = unpack_bf16x2(w.w);
+            *rp = make_uint4(pack_bf16x2(v[8 * i + 0] + a.x, v[8 * i + 1] + a.y),
+                             pack_bf16x2(v[8 * i + 2] + b.x, v[8 * i + 3] + b.y),
+                             pack_bf16x2(v[8 * i + 4] + cc.x, v[8 * i + 5] + cc.y),
+                             pack_bf16x2(v[8 * i + 6] + d.x, v[8 * i + 7] + d.y));
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (n < args.N && lane == 0) tma_store_2d(&tmC, rb, n, box_y);  // warp-uniform column bound
+          if (lane == 0) bulk_commit();
+          ++aux_j;
+        }
       } else if constexpr (EPI == EPI_F32ADD) {
         float* out = reinterpret_cast<float*>(args.out);
         // deterministic split-K: the unit of K chunk q stores its partial into slice q (the
@@ -809,7 +840,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       ++local;
       return true;
     });
-    if constexpr (EPI == EPI_SWIGLU_BWD) {
+    if constexpr (EPI == EPI_SWIGLU_BWD || EPI == EPI_RESIDUAL) {
       // loads issued for chunks that were never consumed (a wait gave up): let them land
       for (int jj = aux_j; jj < aux_loaded; ++jj) mbar_wait(&my_aux_bar[jj & 1], (jj >> 1) & 1);
     }
@@ -1065,6 +1096,10 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
     if (epi == EPI_SWIGLU) {
       TORCH_CHECK(out2.has_value(), "gemm: the SwiGLU epilogue needs its second output");
       mc2 = make_out_map(*out2, M);
+    }
+    if (epi == EPI_RESIDUAL) {  // the residual, loaded as boxes of the output's shape
+      TORCH_CHECK(residual.has_value(), "gemm: the residual epilogue needs its residual");
+      mc2 = make_out_map(*residual, M);
     }
     if (epi == EPI_SWIGLU_BWD) {  // g | u inputs, loaded as boxes of the same shape
       TORCH_CHECK(aux.has_value() && aux->size(1) >= 2 * pair_offset, "gemm: the SwiGLU backward needs g | u");
