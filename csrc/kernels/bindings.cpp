@@ -12,6 +12,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
           const c10::optional<at::Tensor>& ce_tgt, bool stream_k, int64_t splitk,
           const c10::optional<at::Tensor>& jobs);
 void copy_jobs(const at::Tensor& jobs, int64_t device);
+int64_t gemm_balanced_split(int64_t s0, int64_t tiles, int64_t units, int64_t nk);
 void shard_update(const at::Tensor& items, const at::Tensor& buf, const std::vector<int64_t>& offs,
                   const at::Tensor& full_grad, const at::Tensor& shard16, const at::Tensor& ran, int64_t world,
                   int64_t rank, const at::Tensor& hyper, double beta1, double beta2, double wd, double ema_decay);
@@ -63,6 +64,8 @@ bool debug_bounds_build();
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "HRM-Text sm_100a kernels";
   m.def("gemm", &hrm::gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("gemm_balanced_split", &hrm::gemm_balanced_split,
+        "split-K factor chosen for an fp32 weight gradient (L2-sized split s0, tiles, CTA pairs, k-blocks)");
   m.def("copy_jobs", &hrm::copy_jobs, "fused-collective copy jobs (gather / push) without a GEMM to ride on");
   m.def("shard_update", &hrm::shard_update, "step-end inbox reduction + AdamATan2 on this rank's shards");
   m.def("attn_schedule_capacity", &hrm::attn_schedule_capacity);

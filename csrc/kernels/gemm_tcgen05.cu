@@ -1167,6 +1167,12 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   TORCH_CHECK(false, "gemm: unsupported (a_mn, b_mn, epilogue) combination ", a_mn, b_mn, epi);
 }
 
+// The weight-gradient split choice on its own (host arithmetic, no device needed): for tests
+// and for tools that plan launches.
+int64_t gemm_balanced_split(int64_t s0, int64_t tiles, int64_t units, int64_t nk) {
+  return balanced_split((int)s0, tiles, (int)units, nk);
+}
+
 // Fused-collective copy jobs for one launch (collective_jobs.cuh), from a CPU int64 [16]
 // descriptor: {gather: src addresses tensor ptr, dst ptr, rows, cols, rows per rank;
 // push: src ptr, base addresses tensor ptr, inbox offset, inbox slot stride, count offset,
